@@ -1,0 +1,125 @@
+"""ctypes binding of ``libfdwt_b200.so`` (the C ABI declared in ``include/fdwt_b200.h``).
+
+The library is loaded on first use.  There is no fallback: if the shared library is missing
+or the tensors are not on a CUDA device, the call raises.  Status codes other than
+``FDWT_OK`` become ``RuntimeError`` with the library's message.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libfdwt_b200.so")
+
+c_i64p = ctypes.POINTER(ctypes.c_int64)
+c_dblp = ctypes.POINTER(ctypes.c_double)
+c_voidpp = ctypes.POINTER(ctypes.c_void_p)
+
+DTYPES = {torch.float32: 0, torch.float64: 1, torch.float16: 2, torch.bfloat16: 3}
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "fdwt_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "fdwt_last_cuda_error": (ctypes.c_int, []),
+    "fdwt_version": (ctypes.c_int, []),
+    "fdwt_launch_count": (ctypes.c_ulonglong, []),
+    "fdwt_dwt_analysis": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, c_i64p, c_i64p,
+        c_voidpp, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+        ctypes.c_size_t, ctypes.c_void_p]),
+    "fdwt_dwt_analysis_workspace": (ctypes.c_size_t, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, c_i64p, c_i64p, ctypes.c_int]),
+    "fdwt_dwt_synthesis": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_int, c_voidpp, ctypes.c_int64, c_i64p, c_i64p,
+        ctypes.c_void_p, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+        ctypes.c_size_t, ctypes.c_void_p]),
+    "fdwt_dwt_synthesis_workspace": (ctypes.c_size_t, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int64, c_i64p, c_i64p, ctypes.c_int]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build the sm_100a kernels with "
+                        "`python -m pytorch_morlet_fdwt_b200._build` (or __graft_entry__.build())")
+                lib = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(lib, name)
+                    fn.restype, fn.argtypes = res, args
+                _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        lib = load()
+        msg = lib.fdwt_status_string(status).decode()
+        if status == 4:
+            msg += f" (cudaError {lib.fdwt_last_cuda_error()})"
+        raise RuntimeError(f"{what} failed: {msg}")
+
+
+def require_cuda(*tensors) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "pytorch_morlet_fdwt_b200 computes on CUDA tensors only (sm_100a kernels, no CPU "
+                f"fallback); got a tensor on {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPES[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}") from None
+
+
+def stream_of(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def i64_array(values):
+    arr = (ctypes.c_int64 * max(1, len(values)))(*[int(v) for v in values])
+    return arr
+
+
+def f64_array(values):
+    return (ctypes.c_double * max(1, len(values)))(*[float(v) for v in values])
+
+
+def ptr_array(tensors):
+    return (ctypes.c_void_p * max(1, len(tensors)))(
+        *[None if t is None else t.data_ptr() for t in tensors])
+
+
+def workspace(nbytes: int, device: torch.device):
+    if nbytes == 0:
+        return None
+    return torch.empty(int(nbytes), dtype=torch.uint8, device=device)
+
+
+def launch_count() -> int:
+    """Kernels launched by libfdwt_b200.so so far in this process."""
+    return int(load().fdwt_launch_count())

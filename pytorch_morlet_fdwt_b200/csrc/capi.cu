@@ -1,0 +1,75 @@
+// Library-wide C ABI helpers: status strings, per-thread CUDA error, device attributes.
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+
+namespace fdwt {
+
+static thread_local int g_last_cuda_error = 0;
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void set_cuda_error(cudaError_t e) { g_last_cuda_error = static_cast<int>(e); }
+
+int max_smem_optin() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 48 * 1024;
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      v = 48 * 1024;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+int allow_max_dynamic_smem(const void* kernel) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  FDWT_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return FDWT_OK;
+  FDWT_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 max_smem_optin()));
+  done.insert({kernel, dev});
+  return FDWT_OK;
+}
+
+}  // namespace fdwt
+
+extern "C" const char* fdwt_status_string(int status) {
+  switch (status) {
+    case FDWT_OK: return "ok";
+    case FDWT_ERR_INVALID: return "invalid argument";
+    case FDWT_ERR_UNSUPPORTED: return "unsupported configuration";
+    case FDWT_ERR_WORKSPACE: return "workspace missing or too small";
+    case FDWT_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int fdwt_last_cuda_error(void) { return fdwt::g_last_cuda_error; }
+
+extern "C" int fdwt_version(void) { return 100; }
+
+extern "C" unsigned long long fdwt_launch_count(void) {
+  return fdwt::g_launches.load(std::memory_order_relaxed);
+}

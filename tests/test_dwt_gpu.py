@@ -1,0 +1,234 @@
+"""DWT parity on the GPU: sm_100a kernels (through the C ABI) vs the golden fixtures and the
+CPU oracle, plus size-independent properties at the benchmark sizes.
+
+Tolerances: fp64 1e-12 x max|ref| (the reference's pywt tolerance, tests/test_dwt.py:32), fp32
+1e-5 relative to max|ref| (the north-star bound for DWT coefficients), fp16 1e-2, bf16 6e-2
+(the reference's low-precision test, tests/test_dwt.py:82).
+"""
+
+import numpy as np
+import pytest
+import torch
+from torch.autograd import gradcheck, gradgradcheck
+
+import pytorch_morlet_fdwt_b200 as F
+from oracle import dwt_oracle as D
+from tests.golden_data import bank_from_golden, golden
+
+pytestmark = pytest.mark.gpu
+MODES = ["zero", "periodic", "symmetric", "reflect", "periodization"]
+DEV = "cuda"
+
+
+def close(a, b, tol, floor=0.0):
+    """max|a - b| <= tol * max(max|b|, floor): relative to the reference's magnitude, with an
+    absolute floor for the O(1)-scaled golden cases (pywt's own tests use atol=1e-12)."""
+    a = a.detach().double().cpu().numpy() if torch.is_tensor(a) else np.asarray(a)
+    b = b.detach().double().cpu().numpy() if torch.is_tensor(b) else np.asarray(b)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    scale = max(floor, 1e-300, float(np.abs(b).max()) if b.size else 1.0)
+    err = float(np.abs(a - b).max()) if b.size else 0.0
+    assert err <= tol * scale, f"max err {err:.3e} > {tol:.1e} x {scale:.3e}"
+
+
+def gpu(a, dtype=torch.float64):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+@pytest.mark.parametrize("bname", ["haar", "db2", "db4", "rand5"])
+@pytest.mark.parametrize("mode", MODES)
+def test_single_level_vs_golden(bname, mode):
+    g = golden("dwt_single")
+    bank = F.get_filter_bank(bank_from_golden(bname))
+    for n in [1, 2, 3, 7, 16, 33, 100]:
+        key = f"{bname}|{mode}|{n}"
+        x = gpu(g[key + "|x"])
+        a, d = F.dwt(x, bank, mode)
+        close(a, g[key + "|a"], 1e-12, 1.0)
+        close(d, g[key + "|d"], 1e-12, 1.0)
+        xg = x.clone().requires_grad_()
+        a2, d2 = F.dwt(xg, bank, mode)
+        (a2.square().sum() + 3.0 * d2.square().sum()).backward()
+        close(xg.grad, g[key + "|gx"], 1e-12, 1.0)
+        if key + "|y" in g:
+            close(F.idwt(a, d, bank, mode), g[key + "|y"], 1e-12, 1.0)
+            ag, dg = a.clone().requires_grad_(), d.clone().requires_grad_()
+            F.idwt(ag, dg, bank, mode).square().sum().backward()
+            close(ag.grad, g[key + "|ga"], 1e-12, 1.0)
+            close(dg.grad, g[key + "|gd"], 1e-12, 1.0)
+        else:
+            with pytest.raises(ValueError):
+                F.idwt(a, d, bank, mode)
+
+
+def _multi_keys():
+    g = golden("dwt_multi")
+    return sorted({k.rsplit("|", 1)[0] for k in g.files if k.endswith("|x")})
+
+
+@pytest.mark.parametrize("key", _multi_keys())
+def test_multilevel_vs_golden(key):
+    g = golden("dwt_multi")
+    bname, mode, n = key.split("|")
+    bank = F.get_filter_bank(bank_from_golden(bname))
+    level = int(g[key + "|level"])
+    x = gpu(g[key + "|x"]).requires_grad_()
+    coeffs = F.wavedec(x, bank, mode, level)
+    assert len(coeffs) == level + 1
+    for i, c in enumerate(coeffs):
+        close(c, g[key + f"|c{i}"], 1e-12, 1.0)
+    sum((c.square() * (1.0 + i)).sum() for i, c in enumerate(coeffs)).backward()
+    close(x.grad, g[key + "|gx"], 1e-12, 1.0)
+    cs = [gpu(g[key + f"|c{i}"]).requires_grad_() for i in range(level + 1)]
+    y = F.waverec(cs, bank, mode)
+    close(y, g[key + "|y"], 1e-12, 1.0)
+    y.square().sum().backward()
+    for i, c in enumerate(cs):
+        close(c.grad, g[key + f"|gc{i}"], 1e-12, 1.0)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_gradcheck_and_double_backward(mode):
+    torch.manual_seed(0)
+    for wname in ["haar", "db3"]:
+        bank = F.get_filter_bank(wname)
+        for n in [1, 2, 5, 8, 13, 40]:
+            x = torch.randn(2, n, dtype=torch.float64, device=DEV, requires_grad=True)
+            assert gradcheck(lambda t: F.dwt(t, bank, mode), (x,))
+            assert gradgradcheck(lambda t: F.dwt(t, bank, mode), (x,))
+            a, d = (t.detach().requires_grad_() for t in F.dwt(x, bank, mode))
+            if mode == "periodization" or 2 * a.shape[-1] - bank.length + 2 > 0:
+                assert gradcheck(lambda p, q: F.idwt(p, q, bank, mode), (a, d))
+        x = torch.randn(3, 37, dtype=torch.float64, device=DEV, requires_grad=True)
+        assert gradgradcheck(lambda t: F.wavedec(t, bank, mode, 3), (x,))
+
+
+def test_cfg1_wavedec_waverec_fp32():
+    """db4 symmetric level 5 on (32, 64, 2500) fp32, forward + backward of sum c^2."""
+    torch.manual_seed(0)
+    bank = F.get_filter_bank("db4")
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    x = torch.randn(32, 64, 2500, device=DEV).requires_grad_()
+    coeffs = F.wavedec(x, "db4", "symmetric", 5)
+    x64 = x.detach().double().cpu().numpy().reshape(-1, 2500)
+    ref = D.wavedec(x64, tb, "symmetric", 5)
+    for c, r in zip(coeffs, ref):
+        close(c.reshape(-1, c.shape[-1]), r, 1e-5)
+    sum(c.square().sum() for c in coeffs).backward()
+    gref = D.wavedec_vjp(2500, [2 * r for r in ref], tb, "symmetric")
+    close(x.grad.reshape(-1, 2500), gref, 1e-5)
+    y = F.waverec([c.detach() for c in coeffs], "db4", "symmetric")
+    close(y.reshape(-1, y.shape[-1]), D.waverec(ref, tb, "symmetric"), 1e-5)
+    close(y[..., :2500], x.detach(), 1e-5)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_cfg2_long_signal_fp32(mode):
+    """db8 level 8 on (16, 128, 65536) fp32 -- every mode.  Sampled rows against the
+    oracle, every row through size-independent properties (adjointness, reconstruction)."""
+    torch.manual_seed(1)
+    bank = F.get_filter_bank("db8")
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    x = torch.randn(16, 128, 65536, device=DEV)
+    coeffs = F.wavedec(x, bank, mode, 8)
+    rows = [0, 1, 777, 2047]
+    xr = x.reshape(-1, 65536)[rows].double().cpu().numpy()
+    ref = D.wavedec(xr, tb, mode, 8)
+    for c, r in zip(coeffs, ref):
+        close(c.reshape(-1, c.shape[-1])[rows], r, 1e-5)
+    # adjointness <A x, g> == <x, A^T g> on every row (fp64 accumulation of fp32 kernels)
+    gs = [torch.randn_like(c) for c in coeffs]
+    xx = x.clone().requires_grad_()
+    cs = F.wavedec(xx, bank, mode, 8)
+    torch.autograd.backward(cs, gs)
+    lhs = sum((c.double() * g.double()).sum() for c, g in zip(coeffs, gs))
+    rhs = (x.double() * xx.grad.double()).sum()
+    assert abs(float(lhs - rhs)) <= 1e-5 * float(lhs.abs() + rhs.abs())
+    gref = D.wavedec_vjp(65536, [g.reshape(-1, g.shape[-1])[rows].double().cpu().numpy()
+                                 for g in gs], tb, mode)
+    close(xx.grad.reshape(-1, 65536)[rows], gref, 1e-5)
+    # reconstruction and the waverec backward
+    cs2 = [c.detach().requires_grad_() for c in coeffs]
+    y = F.waverec(cs2, bank, mode)
+    close(y.reshape(-1, y.shape[-1])[rows], D.waverec(ref, tb, mode), 1e-5)
+    close(y[..., :65536], x, 1e-5)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    gr = D.waverec_vjp(ref, gy.reshape(-1, y.shape[-1])[rows].double().cpu().numpy(), tb, mode)
+    for c, r in zip(cs2, gr):
+        close(c.grad.reshape(-1, c.shape[-1])[rows], r, 1e-5)
+
+
+def test_long_rows_fp64_multi_segment():
+    """fp64 rows of 65536 do not fit one launch's shared memory: the levels are split into
+    launches that hand the approximation over through the workspace."""
+    torch.manual_seed(2)
+    bank = F.get_filter_bank("db4")
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    for mode in ["symmetric", "periodization"]:
+        x = torch.randn(3, 65536, dtype=torch.float64, device=DEV)
+        coeffs = F.wavedec(x, bank, mode, 10)
+        ref = D.wavedec(x.cpu().numpy(), tb, mode, 10)
+        for c, r in zip(coeffs, ref):
+            close(c, r, 1e-12, 1.0)
+        y = F.waverec(coeffs, bank, mode)
+        close(y, D.waverec(ref, tb, mode), 1e-12, 1.0)
+        xx = x.clone().requires_grad_()
+        sum(c.square().sum() for c in F.wavedec(xx, bank, mode, 10)).backward()
+        close(xx.grad, D.wavedec_vjp(65536, [2 * r for r in ref], tb, mode), 1e-12, 1.0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_low_precision_dtypes(dtype):
+    torch.manual_seed(0)
+    x = torch.randn(4, 1000, device=DEV)
+    ref = F.wavedec(x.double(), "db4", level=4)
+    out = F.wavedec(x.to(dtype), "db4", level=4)
+    tol = {torch.float32: 1e-5, torch.float16: 1e-2, torch.bfloat16: 6e-2}[dtype]
+    for o, r in zip(out, ref):
+        assert o.dtype == dtype
+        torch.testing.assert_close(o.double(), r, atol=tol * r.abs().max().item(), rtol=0)
+    y = F.waverec(out, "db4")
+    assert y.dtype == dtype
+
+
+def test_gpu_matches_oracle_large_batch():
+    torch.manual_seed(0)
+    bank = F.get_filter_bank("db4")
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    x = torch.randn(5, 7, 2049)
+    xg = x.cuda().requires_grad_()
+    outs = F.wavedec(xg, bank, "reflect")
+    ref = D.wavedec(x.double().numpy().reshape(-1, 2049), tb, "reflect")
+    for a, b in zip(outs, ref):
+        close(a.reshape(-1, a.shape[-1]), b, 1e-5)
+    sum((c * c).sum() for c in outs).backward()
+    close(xg.grad.reshape(-1, 2049), D.wavedec_vjp(2049, [2 * r for r in ref], tb, "reflect"), 1e-4)
+
+
+def test_modules_and_errors():
+    x = torch.randn(2, 128, device=DEV)
+    m, im = F.DWT1D("db2", level=3), F.IDWT1D("db2")
+    torch.testing.assert_close(im(m(x))[..., :128], x, atol=1e-5, rtol=1e-5)
+    with pytest.raises(ValueError):
+        F.dwt(x, "morl")
+    with pytest.raises(ValueError):
+        F.dwt(x, "db2", mode="smooth")
+    b = F.get_filter_bank("db2")
+    custom = F.get_filter_bank((b.dec_lo, b.dec_hi, b.rec_lo, b.rec_hi))
+    torch.testing.assert_close(F.dwt(x, custom)[0], F.dwt(x, "db2")[0])
+    assert F.dwt_max_level(1000, "db4") == D.dwt_max_level(1000, 8) == 7
+    assert F.wavedec(x, "db2", level=0)[0] is x
+
+
+def test_empty_batch_and_noncontiguous():
+    x = torch.randn(0, 3, 50, device=DEV)
+    a, d = F.dwt(x, "db2")
+    assert a.shape == (0, 3, 26) and d.shape == (0, 3, 26)
+    base = torch.randn(40, 6, device=DEV, dtype=torch.float64)
+    xt = base.t()  # (6, 40), non-contiguous rows
+    bank = F.get_filter_bank("db2")
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    for c, r in zip(F.wavedec(xt, bank, "symmetric", 2),
+                    D.wavedec(xt.cpu().numpy(), tb, "symmetric", 2)):
+        close(c, r, 1e-12, 1.0)
