@@ -74,11 +74,11 @@ int fdwt_dwt_analysis(int dtype, int64_t rows, const void* x, int64_t n, int lev
                       const double* h0, const double* h1, int filter_len, int mode, int off,
                       void* workspace, size_t workspace_bytes, void* stream);
 
-/* Device workspace (bytes) fdwt_dwt_analysis needs for this problem (0 when every level
- * fits in one launch's shared memory). */
+/* Device workspace (bytes) fdwt_dwt_analysis needs for the same arguments (0 when every
+ * level fits in one launch's shared memory). */
 size_t fdwt_dwt_analysis_workspace(int dtype, int64_t rows, int64_t n, int levels,
                                    const int64_t* coef_len, const int64_t* pad_last,
-                                   int filter_len);
+                                   int filter_len, int mode, int off);
 
 /* Multilevel synthesis: the exact transpose of fdwt_dwt_analysis, level by level from the
  * coarsest.  Level l maps (a, d) -- a = the first coef_len[l-1] samples of the incoming
@@ -99,9 +99,10 @@ int fdwt_dwt_synthesis(int dtype, int64_t rows, int levels, const void* const* i
                        void* y, const double* h0, const double* h1, int filter_len, int mode,
                        int off, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Device workspace (bytes) fdwt_dwt_synthesis needs for the same arguments. */
 size_t fdwt_dwt_synthesis_workspace(int dtype, int64_t rows, int levels, int64_t approx_len,
                                     const int64_t* coef_len, const int64_t* out_len,
-                                    int filter_len);
+                                    int filter_len, int mode, int off);
 
 #ifdef __cplusplus
 }

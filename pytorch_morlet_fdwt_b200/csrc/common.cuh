@@ -74,6 +74,10 @@ __host__ __device__ __forceinline__ int64_t floor_div(int64_t a, int64_t b) {
   return (a % b != 0 && ((a < 0) != (b < 0))) ? q - 1 : q;
 }
 __host__ __device__ __forceinline__ int64_t pos_mod(int64_t a, int64_t b) {
+  if (a >= INT32_MIN && a <= INT32_MAX && b <= INT32_MAX) {  // 32-bit: a short sequence
+    int32_t r = static_cast<int32_t>(a) % static_cast<int32_t>(b);
+    return r < 0 ? r + b : r;
+  }
   int64_t r = a % b;
   return r < 0 ? r + b : r;
 }
@@ -96,8 +100,12 @@ __host__ __device__ __forceinline__ int64_t mode_period(int mode, int64_t n) {
 // Map an extended position p onto [0, n) for a (normalized) mode; returns -1 when the
 // position is outside the signal in zero mode.
 __host__ __device__ __forceinline__ int64_t ext_index(int64_t p, int64_t n, int mode, int64_t P) {
-  if (mode == FDWT_MODE_ZERO) return (p >= 0 && p < n) ? p : -1;
-  int64_t q = pos_mod(p, P);
+  if (p >= 0 && p < n) return p;
+  if (mode == FDWT_MODE_ZERO) return -1;
+  // one wrap covers every extended position of signals longer than the filter; the modulo
+  // (a long dependent sequence for 64-bit operands) is left to the rare multi-wrap case
+  int64_t q = p < 0 ? p + P : (p >= P ? p - P : p);
+  if (q < 0 || q >= P) q = pos_mod(p, P);
   switch (mode) {
     case FDWT_MODE_PERIODIC: return q;
     case FDWT_MODE_SYMMETRIC: return q < n ? q : P - 1 - q;

@@ -98,16 +98,15 @@ extern "C" int fdwt_dwt_analysis(int dtype, int64_t rows, const void* x, int64_t
 
 extern "C" size_t fdwt_dwt_analysis_workspace(int dtype, int64_t rows, int64_t n, int levels,
                                               const int64_t* coef_len, const int64_t* pad_last,
-                                              int filter_len) {
+                                              int filter_len, int mode, int off) {
   const int LM = pick_lm(filter_len);
   if (LM < 0 || rows < 0) return 0;
   std::vector<Level> lv;
-  if (analysis_levels(n, levels, coef_len, pad_last, FDWT_MODE_ZERO, lv, nullptr) != FDWT_OK)
-    return 0;
+  if (analysis_levels(n, levels, coef_len, pad_last, mode, lv, nullptr) != FDWT_OK) return 0;
   size_t need = 0;
   dispatch<true>(dtype, LM, rows, static_cast<const void*>(nullptr), lv,
                    static_cast<void*>(nullptr), static_cast<const double*>(nullptr),
-                   static_cast<const double*>(nullptr), filter_len, 0,
+                   static_cast<const double*>(nullptr), filter_len, off,
                    static_cast<void*>(nullptr), size_t(0), static_cast<cudaStream_t>(nullptr),
                    &need);
   return need;
@@ -133,17 +132,17 @@ extern "C" int fdwt_dwt_synthesis(int dtype, int64_t rows, int levels, const voi
 
 extern "C" size_t fdwt_dwt_synthesis_workspace(int dtype, int64_t rows, int levels,
                                                int64_t approx_len, const int64_t* coef_len,
-                                               const int64_t* out_len, int filter_len) {
+                                               const int64_t* out_len, int filter_len, int mode,
+                                               int off) {
   const int LM = pick_lm(filter_len);
   if (LM < 0 || rows < 0) return 0;
   std::vector<Level> lv;
-  if (synthesis_levels(levels, approx_len, coef_len, out_len, FDWT_MODE_ZERO, lv, nullptr) !=
-      FDWT_OK)
+  if (synthesis_levels(levels, approx_len, coef_len, out_len, mode, lv, nullptr) != FDWT_OK)
     return 0;
   size_t need = 0;
   dispatch<false>(dtype, LM, rows, static_cast<const void*>(nullptr), lv,
                    static_cast<void*>(nullptr), static_cast<const double*>(nullptr),
-                   static_cast<const double*>(nullptr), filter_len, 0,
+                   static_cast<const double*>(nullptr), filter_len, off,
                    static_cast<void*>(nullptr), size_t(0), static_cast<cudaStream_t>(nullptr),
                    &need);
   return need;

@@ -111,7 +111,8 @@ def _analysis(x: torch.Tensor, spec: _Spec) -> List[torch.Tensor]:
     coef, pad = _lib.i64_array(spec.coef_len), _lib.i64_array(spec.pad)
     dt = _lib.dtype_code(x.dtype)
     with torch.cuda.device(dev):
-        nws = lib.fdwt_dwt_analysis_workspace(dt, R, spec.n, J, coef, pad, L)
+        nws = lib.fdwt_dwt_analysis_workspace(dt, R, spec.n, J, coef, pad, L, spec.mode,
+                                               spec.off)
         ws = _lib.workspace(nws, dev)
         st = lib.fdwt_dwt_analysis(
             dt, R, x2.data_ptr(), spec.n, J, coef, pad, _lib.ptr_array(outs),
@@ -141,7 +142,8 @@ def _synthesis(inputs: Sequence[Optional[torch.Tensor]], spec: _Spec) -> torch.T
     outl = _lib.i64_array(spec.in_len)
     dt = _lib.dtype_code(dtype)
     with torch.cuda.device(dev):
-        nws = lib.fdwt_dwt_synthesis_workspace(dt, R, J, spec.approx_len, coef, outl, L)
+        nws = lib.fdwt_dwt_synthesis_workspace(dt, R, J, spec.approx_len, coef, outl, L,
+                                                spec.mode, spec.off)
         ws = _lib.workspace(nws, dev)
         st = lib.fdwt_dwt_synthesis(
             dt, R, J, _lib.ptr_array(rows), spec.approx_len, coef, outl, y.data_ptr(),
