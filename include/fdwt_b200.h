@@ -104,6 +104,60 @@ size_t fdwt_dwt_synthesis_workspace(int dtype, int64_t rows, int levels, int64_t
                                     const int64_t* coef_len, const int64_t* out_len,
                                     int filter_len, int mode, int off);
 
+/* ------------------------------------------------------------------------------------------
+ * Morlet continuous wavelet transform (the a-trous octave pyramid of MorletPlan).
+ *
+ * A plan describes the octaves exactly as the reference's MorletPlan computes them
+ * (fdwt/cwt.py:80-139): octave j holds the scales order[oct_begin[j] .. +oct_count[j]) (global
+ * scale indices, sorted by support) whose filters have 2*oct_half[j]+1 taps at spacing 2^j;
+ * x_j (j >= 1) is the dilated half-band low-pass of x_{j-1} materialised on
+ * [-margins[j], n + margins[j]).  Filters are the (n_scales*channels, 2*center+1) tensor of
+ * MorletPlan.filters (row i*channels + c), read from device memory; scale i uses taps
+ * center-support[i] .. center+support[i] (the rest are zero by construction).
+ * ---------------------------------------------------------------------------------------- */
+#define FDWT_MAX_OCTAVES 24
+#define FDWT_MAX_SCALES 256
+#define FDWT_MAX_LOWPASS 49
+
+typedef struct {
+  int32_t n_octaves;  /* J + 1 */
+  int32_t n_scales;   /* S */
+  int32_t channels;   /* 2: complex Morlet, 1: its real part */
+  int32_t center;     /* filters have 2*center+1 columns */
+  int32_t c_lp;       /* the half-band filter has 2*c_lp+1 taps (0 for a single octave) */
+  int32_t margins[FDWT_MAX_OCTAVES];
+  int32_t oct_half[FDWT_MAX_OCTAVES];   /* 0 when the octave holds no scale */
+  int32_t oct_begin[FDWT_MAX_OCTAVES];
+  int32_t oct_count[FDWT_MAX_OCTAVES];
+  int32_t order[FDWT_MAX_SCALES];
+  int32_t support[FDWT_MAX_SCALES];     /* half-support (taps) of order[k] */
+  double lowpass[FDWT_MAX_LOWPASS];     /* the full half-band filter, 2*c_lp+1 taps */
+} fdwt_morlet_plan;
+
+/* Forward transform: y (rows, n_scales, n, channels) from x (rows, n).  Replaces the
+ * per-octave launches of the forward and half-band launchers (fdwt/kernels/conv.py:306-329,
+ * 411-430) issued by _MorletCWTFunction.forward (fdwt/cwt.py:217-244). */
+int fdwt_cwt_forward(int dtype, int64_t rows, int64_t n, const void* x, const void* filters,
+                     const fdwt_morlet_plan* plan, void* y, void* stream);
+
+/* Fused scalogram mix: y[r, t] = sum_s a[d, s] |W_s[r, t]| + b[d, s] Re W_s[r, t], d = r % dim,
+ * a and b (dim, n_scales); the scalogram is never written.  Replaces mix_forward
+ * (fdwt/kernels/mix.py:74-89) and the half-band chain of _MorletMixFunction.forward
+ * (fdwt/cwt.py:294-320). */
+int fdwt_mix_forward(int dtype, int64_t rows, int64_t n, const void* x, const void* filters,
+                     const fdwt_morlet_plan* plan, const void* a, const void* b, int64_t dim,
+                     void* y, void* stream);
+
+/* Fused spectral softmax: out[r, t] = sum_f softmax_f(|W_f[r, t]| * inv_tau) V_f[r, t] with
+ * V (nch, n_scales) (row r uses V[r % nch]) or, when v_per_position, (rows / nch, n_scales, n)
+ * (row r uses V[r / nch]).  Also writes the softmax max m and denominator l per (r, t) for
+ * the backward pass.  Replaces forward_stage (fdwt/kernels/softmax.py:195-203) and the
+ * octave loop of _SpectralSoftmaxFunction.forward (fdwt/cwt.py:417-450). */
+int fdwt_specsoftmax_forward(int dtype, int64_t rows, int64_t n, const void* x,
+                             const void* filters, const fdwt_morlet_plan* plan, const void* v,
+                             int v_per_position, int64_t nch, double inv_tau, void* out, void* m,
+                             void* l, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

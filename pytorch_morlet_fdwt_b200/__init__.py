@@ -12,12 +12,17 @@ Every transform runs in hand-written CUDA kernels for sm_100a behind the C ABI o
 """
 
 from . import config
+from .cwt import CWT1D, MorletPlan, cwt, freqs_to_scales, scales_to_freqs
 from .dwt import DWT1D, IDWT1D, dwt, dwt_max_level, idwt, wavedec, waverec
+from .layers import (MorletAttention, MorletChannelMixAttention, MorletTokenMixer,
+                     WaveletTokenMixer)
 from .wavelets import FilterBank, get_filter_bank
 
 __version__ = "0.1.0"
 
 __all__ = [
-    "config", "DWT1D", "IDWT1D", "dwt", "dwt_max_level", "idwt", "wavedec", "waverec",
+    "config", "CWT1D", "MorletPlan", "cwt", "freqs_to_scales", "scales_to_freqs",
+    "DWT1D", "IDWT1D", "dwt", "dwt_max_level", "idwt", "wavedec", "waverec",
+    "MorletAttention", "MorletChannelMixAttention", "MorletTokenMixer", "WaveletTokenMixer",
     "FilterBank", "get_filter_bank",
 ]

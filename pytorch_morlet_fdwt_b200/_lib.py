@@ -39,6 +39,17 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_int64, ctypes.c_int, c_voidpp, ctypes.c_int64, c_i64p, c_i64p,
         ctypes.c_void_p, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
         ctypes.c_size_t, ctypes.c_void_p]),
+    "fdwt_cwt_forward": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "fdwt_mix_forward": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_void_p]),
+    "fdwt_specsoftmax_forward": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_double,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "fdwt_dwt_synthesis_workspace": (ctypes.c_size_t, [
         ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int64, c_i64p, c_i64p, ctypes.c_int,
         ctypes.c_int, ctypes.c_int]),

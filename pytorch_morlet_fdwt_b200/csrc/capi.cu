@@ -47,8 +47,10 @@ int allow_max_dynamic_smem(const void* kernel) {
   FDWT_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lock(mu);
   if (done.count({kernel, dev})) return FDWT_OK;
+  cudaFuncAttributes fa{};
+  FDWT_CUDA(cudaFuncGetAttributes(&fa, kernel));
   FDWT_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 max_smem_optin()));
+                                 max_smem_optin() - static_cast<int>(fa.sharedSizeBytes)));
   done.insert({kernel, dev});
   return FDWT_OK;
 }

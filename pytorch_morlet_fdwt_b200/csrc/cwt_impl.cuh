@@ -1,0 +1,620 @@
+// Morlet CWT octave pyramid for sm_100a: forward transform and the two fused scalogram
+// consumers (magnitude/phase mix, online spectral softmax).  Templates; instantiated per
+// element type in cwt_f32.cu / cwt_f64.cu.
+//
+// One CTA owns one signal row.  The pyramid x_0, x_1, ... lives in two ping-pong shared
+// buffers that cover every position a later octave reads; x_j is exactly the reference's
+// zero-padded, margin-truncated signal (fdwt/cwt.py:130-138, 512-519): it is nonzero only on
+// [-e_j, n + e_j) with e_0 = 0 and e_{j+1} = min(margin_{j+1}, e_j + c_lp 2^j), and is stored as
+// zeros elsewhere.  Octave j applies the Morlet filters of its scales at spacing 2^j
+// (fdwt/kernels/conv.py:38-134) and then the dilated half-band step produces x_{j+1}
+// (fdwt/kernels/conv.py:251-279).
+//
+// Filter stage.  A work item is P consecutive polyphase outputs n_i = phi + 2^j (u0 + i) of one
+// phase; the thread keeps a left window x[n_i - 2^j k] and a right window x[n_i + 2^j k] in
+// registers, each advancing with one shared load per tap.  The Morlet filters are even (real
+// part) and odd (imaginary part) in k (fdwt/cwt.py:192-203), so a tap pair costs one packed
+// fp32 FMA per scale: (re, im) += (h_re[k], h_im[k]) * (x_l + x_r, x_l - x_r).  The symmetric
+// and antisymmetric halves of every filter are separated exactly when its coefficient table is
+// built; filters that are not exactly symmetric (never the case for MorletPlan.filters) take a
+// second packed FMA per tap with the antisymmetric halves, so any filter is computed exactly.
+//
+// Epilogues.  STORE writes W (rows, S, n, C) in the user's scale order.  MIX reduces each tile
+// to sum_s a[d,s] |W_s| + b[d,s] Re W_s in registers and accumulates a per-row shared
+// accumulator (no atomics: an item owns its outputs for the whole octave).  SOFTMAX folds
+// |W| / tau into a per-position online softmax (max, denominator, numerator) kept in shared
+// memory across octaves (fdwt/kernels/softmax.py:133-139, 242-247).  Neither writes W.
+#pragma once
+
+#include <algorithm>
+#include <type_traits>
+#include <vector>
+
+#include "common.cuh"
+
+namespace fdwt {
+namespace cwtk {
+
+constexpr int NT = 256;           // threads per CTA
+constexpr int P = 8;              // consecutive polyphase outputs per work item
+constexpr int PS = 3;             // pyramid buffers: one pad element per 8
+constexpr int kMaxOct = FDWT_MAX_OCTAVES;
+constexpr int kMaxScales = FDWT_MAX_SCALES;
+constexpr int kMaxC = (FDWT_MAX_LOWPASS - 1) / 2;
+
+enum Epi { EPI_STORE = 0, EPI_MIX = 1, EPI_SOFTMAX = 2 };
+
+struct Oct {
+  int32_t dil, half, begin, count;
+  int32_t live;  // x_j may be nonzero on [-live, n + live)
+};
+
+template <typename A>
+struct FwdParams {
+  int64_t rows, n;
+  const void* x;    // (rows, n)
+  const void* h;    // filters (S*C, 2*center+1)
+  void* y;          // STORE: (rows, S, n, C); MIX / SOFTMAX: (rows, n)
+  const void* a;    // MIX: (dim, S)        SOFTMAX: V
+  const void* b;    // MIX: (dim, S)
+  void* m_out;      // SOFTMAX: (rows, n)
+  void* l_out;
+  int64_t dim;      // MIX: channels of the a/b tables; SOFTMAX: nch
+  int32_t v_pos;    // SOFTMAX: V per position
+  int32_t n_oct, n_scales, channels, center, c_lp;
+  int32_t ext;      // the pyramid buffers hold positions [-ext, n + ext)
+  int32_t buf_len;  // padded elements of one pyramid buffer
+  int32_t coef_off, extra_off;  // byte offsets of the coefficient table and epilogue state
+  int32_t coef_cap;             // elements of the shared coefficient table (0: taps read from
+                                // global memory, for octaves whose table does not fit)
+  A inv_tau;
+  A lpp[kMaxC + 1];  // lowpass[c_lp + t]
+  A lpm[kMaxC + 1];  // lowpass[c_lp - t]
+  Oct oct[kMaxOct];
+  int32_t order[kMaxScales];
+  int32_t support[kMaxScales];
+};
+
+// ------------------------------------------------------------------------------ helpers
+
+__device__ __forceinline__ unsigned long long pk(float lo, float hi) {
+  return static_cast<unsigned long long>(__float_as_uint(lo)) |
+         (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ float lo_f(unsigned long long v) {
+  return __uint_as_float(static_cast<unsigned>(v));
+}
+__device__ __forceinline__ float hi_f(unsigned long long v) {
+  return __uint_as_float(static_cast<unsigned>(v >> 32));
+}
+__device__ __forceinline__ void ffma2(unsigned long long& acc, unsigned long long a,
+                                      unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+
+// Accumulator pair (re, im) of one scale and output: packed fp32 or two fp64.
+template <typename A>
+struct Acc2;
+template <>
+struct Acc2<float> {
+  unsigned long long v;
+  __device__ __forceinline__ void zero() { v = 0ull; }
+  // (re, im) += (c0, c1) * (s0, s1), c from a 16-byte aligned float pair
+  __device__ __forceinline__ void fma(const float* c, float s0, float s1) {
+    ffma2(v, *reinterpret_cast<const unsigned long long*>(c), pk(s0, s1));
+  }
+  __device__ __forceinline__ float re() const { return lo_f(v); }
+  __device__ __forceinline__ float im() const { return hi_f(v); }
+};
+template <>
+struct Acc2<double> {
+  double r, i;
+  __device__ __forceinline__ void zero() { r = 0.0; i = 0.0; }
+  __device__ __forceinline__ void fma(const double* c, double s0, double s1) {
+    r = ::fma(c[0], s0, r);
+    i = ::fma(c[1], s1, i);
+  }
+  __device__ __forceinline__ double re() const { return r; }
+  __device__ __forceinline__ double im() const { return i; }
+};
+
+// Partition of an octave's `count` scales into blocks of 1..4 (each block shares the pair
+// sums of its tap loop).
+__device__ __forceinline__ int block_size(int rem) {
+  if (rem <= 4) return rem;
+  if (rem == 5 || rem == 6 || rem == 9) return 3;
+  return 4;
+}
+
+// Coefficient table of an octave, per tap k in [0, half] and scale slot s:
+//   [0] sym(re)  = (h_re[c+k] + h_re[c-k]) / 2   (k = 0: h_re[c])
+//   [1] anti(im) = (h_im[c+k] - h_im[c-k]) / 2   (k = 0: 0)
+//   [2] anti(re) = (h_re[c+k] - h_re[c-k]) / 2   (k = 0: 0)
+//   [3] sym(im)  = (h_im[c+k] + h_im[c-k]) / 2   (k = 0: h_im[c])
+// so that  re += [0] (xl + xr) + [2] (xl - xr),  im += [1] (xl - xr) + [3] (xl + xr)  exactly
+// reproduces sum_k h[c+k] x[n - dk] over k = -sup..sup.  Taps beyond a scale's support are 0.
+// Returns (through flags[]) whether each block has nonzero [2]/[3] halves.
+// Folded coefficients of tap k of scale slot s, straight from the filter tensor.
+template <typename A>
+__device__ __forceinline__ void fold_coef(const FwdParams<A>& p, const Oct& O, int s, int k,
+                                          A (&t)[4]) {
+  const A* H = static_cast<const A*>(p.h);
+  const int C = p.channels;
+  const int hcols = 2 * p.center + 1;
+  const int gs = p.order[O.begin + s];
+  const int sup = p.support[O.begin + s];
+  A rp = 0, rm = 0, ip = 0, im = 0;
+  if (k <= sup) {
+    const A* hr = H + static_cast<int64_t>(gs * C) * hcols + p.center;
+    rp = __ldg(hr + k);
+    rm = __ldg(hr - k);
+    if (C == 2) {
+      ip = __ldg(hr + hcols + k);
+      im = __ldg(hr + hcols - k);
+    }
+  }
+  if (k == 0) {
+    t[0] = rp;
+    t[1] = 0;
+    t[2] = 0;
+    t[3] = ip;
+  } else {
+    t[0] = (rp + rm) * A(0.5);
+    t[1] = (ip - im) * A(0.5);
+    t[2] = (rp - rm) * A(0.5);
+    t[3] = (ip + im) * A(0.5);
+  }
+}
+
+template <typename A>
+__device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* flags) {
+  const A* H = static_cast<const A*>(p.h);
+  const int C = p.channels;
+  const int hcols = 2 * p.center + 1;
+  const int cnt = O.count, K = O.half;
+  const int tid = threadIdx.x;
+  if (tid < 8) flags[tid] = 0;
+  __syncthreads();
+  const bool in_smem = cnt * (K + 1) * 4 <= p.coef_cap;
+  for (int w = tid; w < cnt * (K + 1); w += NT) {
+    const int s = w % cnt, k = w / cnt;
+    A t[4];
+    fold_coef<A>(p, O, s, k, t);
+    if (in_smem) {
+      A* d = tab + (k * cnt + s) * 4;
+      d[0] = t[0];
+      d[1] = t[1];
+      d[2] = t[2];
+      d[3] = t[3];
+    }
+    if (t[2] != A(0) || t[3] != A(0)) {
+      int b = 0, s0 = 0;  // which block holds slot s
+      while (s0 + block_size(cnt - s0) <= s) {
+        s0 += block_size(cnt - s0);
+        ++b;
+      }
+      atomicOr(&flags[b], 1);
+    }
+  }
+}
+
+// (re, im) of the SB scales of a block for the item's P outputs.  Coefficients come from the
+// shared table (GTAB = false) or are folded from the global filter tensor per tap (GTAB).
+template <typename A, int SB, bool SYM, bool GTAB>
+__device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
+                                           const A* __restrict__ xb, int phi, int u0, int limit,
+                                           const A* __restrict__ tab, int s0,
+                                           Acc2<A> (&acc)[SB][P]) {
+  const int ext = p.ext, dil = O.dil, K = O.half, cnt = O.count;
+  A L[P], R[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const int pos = min(phi + dil * (u0 + i), limit);
+    L[i] = R[i] = xb[sidx<PS>(pos + ext)];
+  }
+  auto coef = [&](int k, int s, A (&t)[4]) {
+    if (GTAB) {
+      fold_coef<A>(p, O, s0 + s, k, t);
+    } else {
+      const A* c = tab + (k * cnt + s0 + s) * 4;
+      t[0] = c[0];
+      t[1] = c[1];
+      t[2] = c[2];
+      t[3] = c[3];
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < SB; ++s) {
+    alignas(16) A t[4];
+    coef(0, s, t);
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      acc[s][i].zero();
+      acc[s][i].fma(t, L[i], A(0));        // re += h_re[c] x
+      acc[s][i].fma(t + 2, A(0), L[i]);    // im += h_im[c] x
+    }
+  }
+  int pl = phi + dil * (u0 - 1);          // next left load position
+  int pr = phi + dil * (u0 + P);          // next right load position
+  for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
+#pragma unroll
+    for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
+#pragma unroll
+    for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
+    L[0] = xb[sidx<PS>(pl + ext)];
+    R[P - 1] = xb[sidx<PS>(min(pr, limit) + ext)];
+    alignas(16) A t[SB][4];
+#pragma unroll
+    for (int s = 0; s < SB; ++s) coef(k, s, t[s]);
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const A sum = L[i] + R[i], dif = L[i] - R[i];
+#pragma unroll
+      for (int s = 0; s < SB; ++s) {
+        acc[s][i].fma(t[s], sum, dif);
+        if (!SYM) acc[s][i].fma(t[s] + 2, dif, sum);
+      }
+    }
+  }
+}
+
+// One block for one item, then its epilogue.
+template <typename T, typename A, int EPI, int SB, bool SYM>
+__device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, const A* xb,
+                                         const A* tab, int s0, int phi, int u0, int64_t row,
+                                         A (&mix)[P], A (&sm_m)[P], A (&sm_l)[P],
+                                         A (&sm_num)[P]) {
+  const int64_t n = p.n;
+  const int dil = O.dil;
+  const int limit = static_cast<int>(n) + p.ext - 1;  // last buffer position: outputs past
+                                                       // the row end read clamped windows
+  Acc2<A> acc[SB][P];
+  if (O.count * (O.half + 1) * 4 <= p.coef_cap)
+    conv_block<A, SB, SYM, false>(p, O, xb, phi, u0, limit, tab, s0, acc);
+  else
+    conv_block<A, SB, SYM, true>(p, O, xb, phi, u0, limit, tab, s0, acc);
+  const int C = p.channels;
+#pragma unroll
+  for (int s = 0; s < SB; ++s) {
+    const int gs = p.order[O.begin + s0 + s];
+    if (EPI == EPI_STORE) {
+      A* yb = static_cast<A*>(p.y) + ((row * p.n_scales + gs) * n) * C;
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
+        if (ni < n) {
+          if (C == 2) {
+            yb[2 * ni] = acc[s][i].re();
+            yb[2 * ni + 1] = acc[s][i].im();
+          } else {
+            yb[ni] = acc[s][i].re();
+          }
+        }
+      }
+    } else if (EPI == EPI_MIX) {
+      const int64_t d = row % p.dim;
+      const A av = static_cast<const A*>(p.a)[d * p.n_scales + gs];
+      const A bv = static_cast<const A*>(p.b)[d * p.n_scales + gs];
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const A re = acc[s][i].re(), im = acc[s][i].im();
+        const A mag = C == 2 ? sqrt(re * re + im * im) : fabs(re);
+        mix[i] += av * mag + bv * re;
+      }
+    } else {
+      const A* V = static_cast<const A*>(p.a);
+      const int64_t g = row / p.dim, c = row % p.dim;
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
+        const A re = acc[s][i].re(), im = acc[s][i].im();
+        const A a = sqrt(re * re + im * im) * p.inv_tau;
+        A v;
+        if (p.v_pos) v = ni < n ? V[(g * p.n_scales + gs) * n + ni] : A(0);
+        else v = V[c * p.n_scales + gs];
+        const A m_new = fmax(sm_m[i], a);
+        const A alpha = exp(sm_m[i] - m_new);
+        const A e = exp(a - m_new);
+        sm_l[i] = sm_l[i] * alpha + e;
+        sm_num[i] = sm_num[i] * alpha + e * v;
+        sm_m[i] = m_new;
+      }
+    }
+  }
+}
+
+template <typename T, typename A, int EPI, int SB>
+__device__ __forceinline__ void do_block_sym(const FwdParams<A>& p, const Oct& O, const A* xb,
+                                             const A* tab, int s0, bool sym, int phi, int u0,
+                                             int64_t row, A (&mix)[P], A (&sm_m)[P],
+                                             A (&sm_l)[P], A (&sm_num)[P]) {
+  if (sym) do_block<T, A, EPI, SB, true>(p, O, xb, tab, s0, phi, u0, row, mix, sm_m, sm_l, sm_num);
+  else do_block<T, A, EPI, SB, false>(p, O, xb, tab, s0, phi, u0, row, mix, sm_m, sm_l, sm_num);
+}
+
+// Dispatch a block of runtime size 1..4.
+template <typename T, typename A, int EPI>
+__device__ __forceinline__ void run_block(const FwdParams<A>& p, const Oct& O, const A* xb,
+                                          const A* tab, int s0, int sb, bool sym, int phi,
+                                          int u0, int64_t row, A (&mix)[P], A (&sm_m)[P],
+                                          A (&sm_l)[P], A (&sm_num)[P]) {
+  switch (sb) {
+    case 1: do_block_sym<T, A, EPI, 1>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    case 2: do_block_sym<T, A, EPI, 2>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    case 3: do_block_sym<T, A, EPI, 3>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    default: do_block_sym<T, A, EPI, 4>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+  }
+}
+
+// x_{j+1} from x_j (dilation dil), written over the whole buffer range (zero outside live).
+template <typename A>
+__device__ void lowpass_step(const FwdParams<A>& p, const A* cur, A* nxt, int dil, int live) {
+  const int n = static_cast<int>(p.n);
+  const int ext = p.ext;
+  const int c = p.c_lp;
+  for (int q = threadIdx.x - ext; q < n + ext; q += NT) {
+    A v = A(0);
+    if (q >= -live && q < n + live) {
+      v = p.lpp[0] * cur[sidx<PS>(q + ext)];
+      for (int t = 1; t <= c; ++t) {
+        v = fma(p.lpp[t], cur[sidx<PS>(q - dil * t + ext)], v);
+        v = fma(p.lpm[t], cur[sidx<PS>(q + dil * t + ext)], v);
+      }
+    }
+    nxt[sidx<PS>(q + ext)] = v;
+  }
+}
+
+template <typename T, typename A, int EPI>
+__global__ void __launch_bounds__(NT)
+cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  A* buf0 = reinterpret_cast<A*>(smem);
+  A* buf1 = buf0 + p.buf_len;
+  A* tab = reinterpret_cast<A*>(smem + p.coef_off);
+  A* extra = reinterpret_cast<A*>(smem + p.extra_off);
+  __shared__ int flags[8];
+  const int64_t row = blockIdx.x;
+  const int n = static_cast<int>(p.n);
+  const int ext = p.ext;
+  const int tid = threadIdx.x;
+
+  const T* xr = static_cast<const T*>(p.x) + row * p.n;
+  for (int i = tid; i < n + 2 * ext; i += NT) {
+    const int q = i - ext;
+    buf0[sidx<PS>(i)] = (q >= 0 && q < n) ? to_acc<T>(xr[q]) : A(0);
+  }
+  if (EPI == EPI_MIX) {
+    for (int i = tid; i < n; i += NT) extra[i] = A(0);
+  } else if (EPI == EPI_SOFTMAX) {
+    for (int i = tid; i < n; i += NT) {
+      extra[i] = -INFINITY;
+      extra[n + i] = A(0);
+      extra[2 * n + i] = A(0);
+    }
+  }
+  __syncthreads();
+
+  A* cur = buf0;
+  A* nxt = buf1;
+  for (int j = 0; j < p.n_oct; ++j) {
+    const Oct& O = p.oct[j];
+    if (O.count > 0) {
+      build_coef<A>(p, O, tab, flags);
+      __syncthreads();
+      const int dil = O.dil;
+      const int runs = (static_cast<int>((p.n + dil - 1) / dil) + P - 1) / P;
+      const int items = dil * runs;
+      int nblk = 0;
+      for (int s0 = 0; s0 < O.count; s0 += block_size(O.count - s0)) ++nblk;
+      if (EPI == EPI_STORE) {
+        // spread (block, item) pairs over the threads
+        for (int w = tid; w < nblk * items; w += NT) {
+          const int blk = w / items, it = w % items;
+          int s0 = 0;
+          for (int b = 0; b < blk; ++b) s0 += block_size(O.count - s0);
+          const int phi = it % dil, u0 = (it / dil) * P;
+          if (phi >= n) continue;
+          A mix[P], m_[P], l_[P], num_[P];
+          run_block<T, A, EPI>(p, O, cur, tab, s0, block_size(O.count - s0), flags[blk] == 0,
+                               phi, u0, row, mix, m_, l_, num_);
+        }
+      } else {
+        for (int it = tid; it < items; it += NT) {
+          const int phi = it % dil, u0 = (it / dil) * P;
+          if (phi >= n) continue;
+          A mix[P], sm_m[P], sm_l[P], sm_num[P];
+#pragma unroll
+          for (int i = 0; i < P; ++i) {
+            const int ni = phi + dil * (u0 + i);
+            mix[i] = A(0);
+            if (EPI == EPI_SOFTMAX && ni < n) {
+              sm_m[i] = extra[ni];
+              sm_l[i] = extra[n + ni];
+              sm_num[i] = extra[2 * n + ni];
+            } else {
+              sm_m[i] = -INFINITY;
+              sm_l[i] = A(0);
+              sm_num[i] = A(0);
+            }
+          }
+          int s0 = 0;
+          for (int b = 0; b < nblk; ++b) {
+            const int sb = block_size(O.count - s0);
+            run_block<T, A, EPI>(p, O, cur, tab, s0, sb, flags[b] == 0, phi, u0, row, mix,
+                                 sm_m, sm_l, sm_num);
+            s0 += sb;
+          }
+#pragma unroll
+          for (int i = 0; i < P; ++i) {
+            const int ni = phi + dil * (u0 + i);
+            if (ni < n) {
+              if (EPI == EPI_MIX) {
+                extra[ni] += mix[i];
+              } else {
+                extra[ni] = sm_m[i];
+                extra[n + ni] = sm_l[i];
+                extra[2 * n + ni] = sm_num[i];
+              }
+            }
+          }
+        }
+      }
+      __syncthreads();
+    }
+    if (j + 1 < p.n_oct) {
+      lowpass_step<A>(p, cur, nxt, O.dil, p.oct[j + 1].live);
+      __syncthreads();
+      A* t = cur;
+      cur = nxt;
+      nxt = t;
+    }
+  }
+
+  if (EPI == EPI_MIX) {
+    A* yr = static_cast<A*>(p.y) + row * p.n;
+    for (int i = tid; i < n; i += NT) yr[i] = extra[i];
+  } else if (EPI == EPI_SOFTMAX) {
+    A* o = static_cast<A*>(p.y) + row * p.n;
+    A* mo = static_cast<A*>(p.m_out) + row * p.n;
+    A* lo = static_cast<A*>(p.l_out) + row * p.n;
+    for (int i = tid; i < n; i += NT) {
+      const A l = extra[n + i];
+      o[i] = extra[2 * n + i] / l;
+      mo[i] = extra[i];
+      lo[i] = l;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------ host
+
+struct Geometry {
+  int ext;            // buffer reach
+  std::vector<int> live;
+};
+
+inline int check_plan(const fdwt_morlet_plan* pl, int64_t n) {
+  if (pl == nullptr) return FDWT_ERR_INVALID;
+  if (pl->n_octaves < 1 || pl->n_octaves > kMaxOct) return FDWT_ERR_INVALID;
+  if (pl->n_scales < 1 || pl->n_scales > kMaxScales) return FDWT_ERR_INVALID;
+  if (pl->channels != 1 && pl->channels != 2) return FDWT_ERR_INVALID;
+  if (pl->c_lp < 0 || pl->c_lp > kMaxC) return FDWT_ERR_UNSUPPORTED;
+  if (pl->n_octaves > 1 && pl->c_lp < 1) return FDWT_ERR_INVALID;
+  if (n < 1) return FDWT_ERR_INVALID;
+  int total = 0;
+  for (int j = 0; j < pl->n_octaves; ++j) {
+    if (pl->oct_count[j] < 0 || pl->oct_half[j] < 0 || pl->oct_half[j] > pl->center)
+      return FDWT_ERR_INVALID;
+    if (pl->oct_count[j] > 0 && pl->oct_begin[j] + pl->oct_count[j] > pl->n_scales)
+      return FDWT_ERR_INVALID;
+    total += pl->oct_count[j];
+    for (int s = 0; s < pl->oct_count[j]; ++s) {
+      const int k = pl->oct_begin[j] + s;
+      if (pl->order[k] < 0 || pl->order[k] >= pl->n_scales) return FDWT_ERR_INVALID;
+      if (pl->support[k] < 0 || pl->support[k] > pl->oct_half[j]) return FDWT_ERR_INVALID;
+    }
+  }
+  if (total != pl->n_scales) return FDWT_ERR_INVALID;
+  return FDWT_OK;
+}
+
+inline Geometry geometry(const fdwt_morlet_plan* pl) {
+  Geometry g;
+  const int J = pl->n_octaves;
+  g.live.assign(J, 0);
+  for (int j = 0; j + 1 < J; ++j)
+    g.live[j + 1] = std::min(pl->margins[j + 1], g.live[j] + pl->c_lp * (1 << j));
+  int ext = 0;
+  for (int j = 0; j < J; ++j) {
+    const int dil = 1 << j;
+    if (pl->oct_count[j] > 0) ext = std::max(ext, pl->oct_half[j] * dil);
+    ext = std::max(ext, g.live[j]);
+    if (j + 1 < J) ext = std::max(ext, g.live[j + 1] + pl->c_lp * dil);
+  }
+  g.ext = ext + 8;
+  return g;
+}
+
+template <typename A>
+void fill_common(FwdParams<A>& p, const fdwt_morlet_plan* pl, const Geometry& g, int64_t n) {
+  p.n = n;
+  p.n_oct = pl->n_octaves;
+  p.n_scales = pl->n_scales;
+  p.channels = pl->channels;
+  p.center = pl->center;
+  p.c_lp = pl->c_lp;
+  p.ext = g.ext;
+  for (int t = 0; t <= kMaxC; ++t) {
+    p.lpp[t] = t <= pl->c_lp ? static_cast<A>(pl->lowpass[pl->c_lp + t]) : A(0);
+    p.lpm[t] = t <= pl->c_lp ? static_cast<A>(pl->lowpass[pl->c_lp - t]) : A(0);
+  }
+  for (int j = 0; j < pl->n_octaves; ++j) {
+    p.oct[j].dil = 1 << j;
+    p.oct[j].half = pl->oct_half[j];
+    p.oct[j].begin = pl->oct_begin[j];
+    p.oct[j].count = pl->oct_count[j];
+    p.oct[j].live = g.live[j];
+  }
+  for (int k = 0; k < pl->n_scales; ++k) {
+    p.order[k] = pl->order[k];
+    p.support[k] = pl->support[k];
+  }
+}
+
+template <typename T, typename A, int EPI>
+int run_forward(int64_t rows, int64_t n, const void* x, const void* h,
+                const fdwt_morlet_plan* pl, void* y, const void* a, const void* b,
+                void* m_out, void* l_out, int64_t dim, int v_pos, double inv_tau,
+                cudaStream_t stream) {
+  int st = check_plan(pl, n);
+  if (st != FDWT_OK) return st;
+  if (rows == 0) return FDWT_OK;
+  if (rows > 0x7fffffffLL || n > 0x3fffffffLL) return FDWT_ERR_UNSUPPORTED;
+  const Geometry g = geometry(pl);
+  FwdParams<A> p{};
+  fill_common(p, pl, g, n);
+  p.rows = rows;
+  p.x = x;
+  p.h = h;
+  p.y = y;
+  p.a = a;
+  p.b = b;
+  p.m_out = m_out;
+  p.l_out = l_out;
+  p.dim = dim;
+  p.v_pos = v_pos;
+  p.inv_tau = static_cast<A>(inv_tau);
+  const int64_t span = n + 2 * static_cast<int64_t>(g.ext);
+  p.buf_len = static_cast<int>(padded_len<PS>(span) + 8);
+  // the coefficient table takes what is left of the shared budget (up to the largest octave)
+  int coef = 0;
+  for (int j = 0; j < pl->n_octaves; ++j)
+    coef = std::max(coef, pl->oct_count[j] * (pl->oct_half[j] + 1) * 4);
+  const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
+  const size_t fixed = 2 * static_cast<size_t>(p.buf_len) * sizeof(A) + 64 +
+      (EPI == EPI_MIX ? 1 : EPI == EPI_SOFTMAX ? 3 : 0) * static_cast<size_t>(n) * sizeof(A);
+  if (fixed > budget) return FDWT_ERR_UNSUPPORTED;
+  const size_t room = (budget - fixed) / sizeof(A);
+  if (static_cast<size_t>(coef) > room) coef = static_cast<int>(room / 4 * 4);
+  coef = std::min(coef, 24 * 1024 / static_cast<int>(sizeof(A)) * 4);  // keep occupancy
+  p.coef_cap = coef;
+  size_t off = 2 * static_cast<size_t>(p.buf_len) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  p.coef_off = static_cast<int>(off);
+  off += static_cast<size_t>(coef) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  p.extra_off = static_cast<int>(off);
+  if (EPI == EPI_MIX) off += static_cast<size_t>(n) * sizeof(A);
+  if (EPI == EPI_SOFTMAX) off += 3 * static_cast<size_t>(n) * sizeof(A);
+  const size_t smem = off + 16;
+  if (smem > budget) return FDWT_ERR_UNSUPPORTED;
+  auto kern = cwt_forward_kernel<T, A, EPI>;
+  st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
+  if (st != FDWT_OK) return st;
+  kern<<<static_cast<unsigned>(rows), NT, smem, stream>>>(p);
+  return launch_status();
+}
+
+}  // namespace cwtk
+}  // namespace fdwt

@@ -1,0 +1,467 @@
+"""Continuous wavelet transform with the (complex) Morlet wavelet, on sm_100a kernels.
+
+    W[s, n] = sum_m x[m] * conj(psi((m - n) / s)) / norm(s)
+    psi(t)  = pi^(-1/4) * (exp(i*w0*t) - exp(-w0^2/2)) * exp(-t^2/2)
+
+Same API and numbers as the reference's ``fdwt/cwt.py``: ``cwt``, ``CWT1D``, ``MorletPlan``,
+``freqs_to_scales``, ``scales_to_freqs``, the fused consumers ``morlet_mix`` and
+``spectral_softmax``, and the private names tests touch (``_apply_plan``,
+``_MorletMixFunction.MIX_CHUNK_BYTES``, ``_SpectralSoftmaxFunction.CHUNK_BYTES``).
+
+``method="fast"`` (octave pyramid) and ``"direct"`` (one octave, exact supports) run the
+row-resident pyramid kernels of ``libfdwt_b200.so`` (``fdwt_cwt_forward`` & co. in
+``include/fdwt_b200.h``): one launch computes every octave, the half-band chain stays in shared
+memory, and the mixers never write the scalogram.  ``method="fft"`` applies the same filters
+through cuFFT (``torch.fft``), as the reference does.  Inputs must be CUDA tensors.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from functools import lru_cache
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+from torch import nn
+
+from . import _lib
+
+__all__ = ["cwt", "CWT1D", "MorletPlan", "freqs_to_scales", "scales_to_freqs", "morlet_mix",
+           "spectral_softmax"]
+
+_PI_M14 = math.pi ** -0.25
+_MAX_OCT, _MAX_SCALES, _MAX_LP = 24, 256, 49
+
+
+def freqs_to_scales(freqs, fs: float = 1.0, w0: float = 6.0) -> torch.Tensor:
+    """Scale (in samples) whose Morlet centre frequency is ``freqs`` (same unit as ``fs``)."""
+    f = torch.as_tensor(freqs, dtype=torch.float64)
+    return w0 * fs / (2 * math.pi * f)
+
+
+def scales_to_freqs(scales, fs: float = 1.0, w0: float = 6.0) -> torch.Tensor:
+    s = torch.as_tensor(scales, dtype=torch.float64)
+    return w0 * fs / (2 * math.pi * s)
+
+
+def _halfband(c: int, beta: float) -> torch.Tensor:
+    """Kaiser-windowed half-band low-pass, 2c+1 taps, unit DC gain (``fdwt/cwt.py:65-68``)."""
+    n = torch.arange(-c, c + 1, dtype=torch.float64)
+    h = 0.5 * torch.sinc(n / 2) * torch.from_numpy(np.kaiser(2 * c + 1, beta))
+    return h / h.sum()
+
+
+def _next_pow2(v: int) -> int:
+    return 1 if v <= 1 else 1 << (int(v) - 1).bit_length()
+
+
+@dataclass
+class _Stage:
+    octave: int
+    dil: int                # filter dilation 2**octave
+    scale_idx: List[int]    # global scale indices, sorted by support
+    half: int               # filters have 2*half+1 taps (at spacing `dil`)
+    support: List[int]      # per scale half-support (taps)
+
+
+class _PlanC(ctypes.Structure):
+    """ctypes mirror of ``fdwt_morlet_plan`` (include/fdwt_b200.h)."""
+
+    _fields_ = [("n_octaves", ctypes.c_int32), ("n_scales", ctypes.c_int32),
+                ("channels", ctypes.c_int32), ("center", ctypes.c_int32),
+                ("c_lp", ctypes.c_int32),
+                ("margins", ctypes.c_int32 * _MAX_OCT), ("oct_half", ctypes.c_int32 * _MAX_OCT),
+                ("oct_begin", ctypes.c_int32 * _MAX_OCT), ("oct_count", ctypes.c_int32 * _MAX_OCT),
+                ("order", ctypes.c_int32 * _MAX_SCALES), ("support", ctypes.c_int32 * _MAX_SCALES),
+                ("lowpass", ctypes.c_double * _MAX_LP)]
+
+
+class MorletPlan:
+    """Static description of a Morlet CWT: scale grouping, filter sizes and margins.
+
+    Reproduces the reference's ``MorletPlan`` (``fdwt/cwt.py:80-203``) exactly: octave j holds
+    the scales in ``[2^j s_th, 2^(j+1) s_th)`` with ``s_th = (w0 + truncate) / (0.8 pi)``;
+    supports are ``ceil(truncate * support_margin * s / 2^j)``; the half-band filter has 33
+    (or 49 when ``truncate > 4.5``) taps; ``x_j`` is materialised on ``[-m_j, N + m_j)``.
+    """
+
+    def __init__(self, scales: Sequence[float], w0: float = 6.0, truncate: float = 4.0,
+                 norm: str = "l2", complex: bool = True, method: str = "fast",
+                 support_margin: float = 1.0):
+        if method not in ("fast", "direct", "fft"):
+            raise ValueError(f"unknown method '{method}' (expected 'fast', 'direct' or 'fft')")
+        if norm not in ("l1", "l2"):
+            raise ValueError("norm must be 'l1' or 'l2'")
+        scales = [float(s) for s in scales]
+        if not scales or min(scales) <= 0:
+            raise ValueError("scales must be a non-empty sequence of positive numbers")
+        self.scales, self.w0, self.truncate, self.norm = scales, float(w0), float(truncate), norm
+        self.complex, self.method = bool(complex), method
+        self.channels = 2 if complex else 1
+        reach = truncate * support_margin
+
+        self.s_th = (w0 + truncate) / (0.8 * math.pi)
+        groups: Dict[int, List[int]] = {}
+        for i, s in enumerate(scales):
+            j = 0 if method != "fast" else max(0, math.floor(math.log2(s / self.s_th)))
+            groups.setdefault(j, []).append(i)
+        self.stages: List[_Stage] = []
+        for j in sorted(groups):
+            dil = 2 ** j
+            sup = {i: max(1, math.ceil(reach * scales[i] / dil)) for i in groups[j]}
+            idx = sorted(groups[j], key=lambda i: sup[i])
+            self.stages.append(_Stage(j, dil, idx, max(sup.values()), [sup[i] for i in idx]))
+        self.n_octaves = self.stages[-1].octave + 1
+        self.center = max(st.half for st in self.stages)
+        self._dil = [0.0] * len(scales)
+        self._sup = [0.0] * len(scales)
+        for st in self.stages:
+            for i, c in zip(st.scale_idx, st.support):
+                self._dil[i], self._sup[i] = float(st.dil), float(c)
+
+        c_lp, beta = (16, 8.0) if truncate <= 4.5 else (24, 10.0)
+        multi = self.n_octaves > 1
+        self.lowpass = _halfband(c_lp, beta) if multi else torch.zeros(1, dtype=torch.float64)
+        self.c_lp = c_lp if multi else 0
+
+        J = self.n_octaves - 1
+        by_oct = {st.octave: st for st in self.stages}
+        self.margins = [0] * (J + 1)
+        for j in range(J, 0, -1):
+            own = by_oct[j].half * 2 ** j if j in by_oct else 0
+            nxt = self.margins[j + 1] + self.c_lp * 2 ** j if j < J else 0
+            self.margins[j] = max(own, nxt)
+        self._static_cache: Dict = {}
+        self._capi_struct = None
+
+    @property
+    def num_scales(self) -> int:
+        return len(self.scales)
+
+    def halfband_taps(self, device, dtype) -> torch.Tensor:
+        """``taps[t] = lowpass[c_lp + t]`` (t = 0..c_lp), as the reference exposes it."""
+        key = ("hb", torch.device(device), dtype)
+        if key not in self._static_cache:
+            self._static_cache[key] = self.lowpass[self.c_lp:].to(device=device, dtype=dtype)
+        return self._static_cache[key]
+
+    def filters(self, scales: torch.Tensor, w0, dtype: torch.dtype) -> torch.Tensor:
+        """All sampled Morlet filters as one ``(S*C, 2*center+1)`` tensor (row ``i*C + c``).
+
+        Scale ``i`` is sampled with the spacing (dilation) of its octave and truncated to its
+        support.  Differentiable w.r.t. ``scales`` and ``w0`` (when it is a tensor).  Same
+        expression as the reference (``fdwt/cwt.py:181-203``).
+        """
+        dev = scales.device
+        f64 = torch.float64
+        s = scales.to(f64)[:, None]
+        dil = torch.tensor(self._dil, dtype=f64, device=dev)[:, None]
+        sup = torch.tensor(self._sup, dtype=f64, device=dev)[:, None]
+        k = torch.arange(-self.center, self.center + 1, device=dev, dtype=f64)[None, :]
+        t = k * dil / s
+        env = torch.exp(-0.5 * t * t) * (k.abs() <= sup)
+        amp = _PI_M14 * dil / (s.sqrt() if self.norm == "l2" else s)
+        w0_ = torch.as_tensor(w0, dtype=f64, device=dev)
+        w0t = w0_ * t
+        re = (torch.cos(w0t) - torch.exp(-0.5 * w0_ * w0_)) * env * amp
+        if not self.complex:
+            return re.to(dtype)
+        im = torch.sin(w0t) * env * amp
+        return torch.stack([re, im], 1).reshape(-1, k.shape[1]).to(dtype)
+
+    def capi(self) -> _PlanC:
+        """The plan as the C struct the kernels take (built once)."""
+        if self._capi_struct is None:
+            if self.n_octaves > _MAX_OCT or self.num_scales > _MAX_SCALES:
+                raise ValueError(f"the sm_100a kernels support up to {_MAX_OCT} octaves and "
+                                 f"{_MAX_SCALES} scales")
+            c = _PlanC()
+            c.n_octaves, c.n_scales = self.n_octaves, self.num_scales
+            c.channels, c.center, c.c_lp = self.channels, self.center, self.c_lp
+            for j, m in enumerate(self.margins):
+                c.margins[j] = m
+            k = 0
+            for st in self.stages:
+                c.oct_half[st.octave] = st.half
+                c.oct_begin[st.octave] = k
+                c.oct_count[st.octave] = len(st.scale_idx)
+                for i, sup in zip(st.scale_idx, st.support):
+                    c.order[k], c.support[k] = i, sup
+                    k += 1
+            lp = self.lowpass.tolist()
+            for t, v in enumerate(lp[:_MAX_LP]):
+                c.lowpass[t] = v
+            self._capi_struct = c
+        return self._capi_struct
+
+
+# --------------------------------------------------------------------------- kernel calls
+
+
+def _out_dtype(dtype: torch.dtype) -> torch.dtype:
+    return torch.float64 if dtype == torch.float64 else torch.float32
+
+
+def _filters_on(H: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    return H.detach().to(device=x.device, dtype=x.dtype).contiguous()
+
+
+def _cwt_forward(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor) -> torch.Tensor:
+    """Rows ``x (R, N)`` (fp32/fp64) -> ``y (R, S, N, C)``."""
+    dev = _lib.require_cuda(x, H)
+    lib = _lib.load()
+    R, N = x.shape
+    y = torch.empty((R, plan.num_scales, N, plan.channels), device=dev, dtype=x.dtype)
+    Hd = _filters_on(H, x)
+    with torch.cuda.device(dev):
+        st = lib.fdwt_cwt_forward(_lib.dtype_code(x.dtype), R, N, x.data_ptr(), Hd.data_ptr(),
+                                  ctypes.addressof(plan.capi()), y.data_ptr(), _lib.stream_of(dev))
+    _lib.check(st, "fdwt_cwt_forward")
+    return y
+
+
+class _MorletCWTFunction(torch.autograd.Function):
+    """All octaves of the transform in one autograd node (``fdwt/cwt.py:213-281``)."""
+
+    @staticmethod
+    def forward(ctx, x, plan: MorletPlan, H):
+        ctx.plan = plan
+        ctx.save_for_backward(x, H)
+        return _cwt_forward(x, plan, H)
+
+    @staticmethod
+    def backward(ctx, g):
+        raise NotImplementedError("CWT backward kernels are not built yet")
+
+
+def _fft_transform(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor) -> torch.Tensor:
+    """``method="fft"``: the direct filters applied through cuFFT (``fdwt/cwt.py:586-594``)."""
+    R, N = x.shape
+    C = plan.channels
+    out = x.new_zeros((R, plan.num_scales, N, C))
+    for st in plan.stages:
+        rows = [i * C + c for i in st.scale_idx for c in range(C)]
+        h = H[rows][:, plan.center - st.half: plan.center + st.half + 1].to(x.dtype)
+        K = h.shape[1]
+        nfft = 1 << (N + K - 1 - 1).bit_length()
+        X = torch.fft.rfft(x, nfft)
+        Hf = torch.fft.rfft(h, nfft)
+        y = torch.fft.irfft(X[:, None, :] * Hf[None], nfft)[..., st.half:st.half + N]
+        y = y.reshape(R, len(st.scale_idx), C, N).transpose(-1, -2)
+        out = out.index_copy(1, torch.tensor(st.scale_idx, device=x.device), y)
+    return out
+
+
+def _apply_plan(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor) -> torch.Tensor:
+    """``x (..., N)`` -> ``(..., S, N)`` complex (real if ``plan.complex`` is False)."""
+    if not x.is_floating_point() or x.is_complex():
+        raise TypeError("cwt expects a real floating point tensor")
+    _lib.require_cuda(x)
+    lead, N = x.shape[:-1], x.shape[-1]
+    x2 = x.reshape(-1, N).contiguous()
+    if x2.dtype not in (torch.float32, torch.float64):
+        x2 = x2.float()
+    if plan.method == "fft":
+        y = _fft_transform(x2, plan, H.to(x2.dtype))
+    else:
+        y = _MorletCWTFunction.apply(x2, plan, H)
+    y = y.reshape(*lead, plan.num_scales, N, plan.channels)
+    return torch.view_as_complex(y) if plan.complex else y[..., 0]
+
+
+@lru_cache(maxsize=64)
+def _cached_plan(scales: Tuple[float, ...], w0, truncate, norm, complex, method) -> MorletPlan:
+    return MorletPlan(scales, w0, truncate, norm, complex, method)
+
+
+@lru_cache(maxsize=64)
+def _cached_filters(plan: MorletPlan, device: torch.device, dtype: torch.dtype):
+    s = torch.tensor(plan.scales, dtype=torch.float64, device=device)
+    return plan.filters(s, plan.w0, dtype)
+
+
+def _resolve_scales(scales, freqs, fs, w0) -> List[float]:
+    if (scales is None) == (freqs is None):
+        raise ValueError("pass exactly one of `scales` or `freqs`")
+    s = freqs_to_scales(freqs, fs, w0) if freqs is not None else torch.as_tensor(
+        scales, dtype=torch.float64)
+    return [float(v) for v in s.flatten()]
+
+
+def cwt(x: torch.Tensor, scales: Optional[Sequence[float]] = None, *, freqs=None, fs: float = 1.0,
+        w0: float = 6.0, method: str = "fast", norm: str = "l2", complex: bool = True,
+        truncate: float = 4.0) -> torch.Tensor:
+    """Morlet CWT along the last dimension: ``(..., N)`` -> ``(..., S, N)`` complex."""
+    s = _resolve_scales(scales, freqs, fs, w0)
+    plan = _cached_plan(tuple(s), float(w0), float(truncate), norm, bool(complex), method)
+    dt = torch.float64 if x.dtype == torch.float64 else torch.float32
+    return _apply_plan(x, plan, _cached_filters(plan, x.device, dt))
+
+
+class CWT1D(nn.Module):
+    """Morlet continuous wavelet transform as a module (``fdwt/cwt.py:654-716``).
+
+    Input ``(..., N)`` real, output ``(..., S, N)`` complex (or real with ``complex=False``).
+    With ``learnable=True`` the (log-)scales are parameters; ``learnable_w0`` also learns the
+    Morlet wave number.
+    """
+
+    def __init__(self, freqs=None, scales=None, fs: float = 1.0, w0: float = 6.0,
+                 method: str = "fast", norm: str = "l2", complex: bool = True,
+                 truncate: float = 4.0, learnable: bool = False, learnable_w0: bool = False,
+                 support_margin: Optional[float] = None):
+        super().__init__()
+        s = _resolve_scales(scales, freqs, fs, w0)
+        if support_margin is None:
+            support_margin = 1.25 if learnable else 1.0
+        self.fs = fs
+        self.plan = MorletPlan(s, w0, truncate, norm, complex, method, support_margin)
+        log_s = torch.tensor(s, dtype=torch.float64).log().float()
+        if learnable:
+            self.log_scales = nn.Parameter(log_s)
+        else:
+            self.register_buffer("log_scales", log_s)
+        if learnable_w0:
+            self.w0 = nn.Parameter(torch.tensor(float(w0)))
+        else:
+            self.w0 = float(w0)
+        self._learn = learnable or learnable_w0
+        self._filter_cache: Dict = {}
+
+    @property
+    def scales(self) -> torch.Tensor:
+        return self.log_scales.exp()
+
+    @property
+    def w0_value(self) -> float:
+        return float(self.w0.detach()) if isinstance(self.w0, torch.Tensor) else float(self.w0)
+
+    @property
+    def freqs(self) -> torch.Tensor:
+        return scales_to_freqs(self.scales.detach(), self.fs, self.w0_value)
+
+    def _filters(self, device, dtype):
+        if self._learn:
+            return self.plan.filters(self.log_scales.to(torch.float64).exp(), self.w0, dtype)
+        key = (device, dtype)
+        if key not in self._filter_cache:
+            self._filter_cache = {key: self.plan.filters(self.scales.to(torch.float64), self.w0,
+                                                         dtype)}
+        return self._filter_cache[key]
+
+    def _apply(self, fn, *args, **kwargs):
+        self._filter_cache = {}
+        return super()._apply(fn, *args, **kwargs)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dt = torch.float64 if x.dtype == torch.float64 else torch.float32
+        return _apply_plan(x, self.plan, self._filters(x.device, dt))
+
+    def extra_repr(self) -> str:
+        p = self.plan
+        return (f"scales={p.num_scales}, w0={self.w0_value:g}, method={p.method}, norm={p.norm}, "
+                f"complex={p.complex}, octaves={p.n_octaves}, learnable={self._learn}")
+
+
+# --------------------------------------------------------------------------- fused consumers
+
+
+def _mix_forward(x2, plan, H, a, b):
+    dev = _lib.require_cuda(x2, H, a, b)
+    lib = _lib.load()
+    R, N = x2.shape
+    y = torch.empty((R, N), device=dev, dtype=x2.dtype)
+    Hd = _filters_on(H, x2)
+    a_ = a.detach().to(x2.dtype).contiguous()
+    b_ = b.detach().to(x2.dtype).contiguous()
+    with torch.cuda.device(dev):
+        st = lib.fdwt_mix_forward(_lib.dtype_code(x2.dtype), R, N, x2.data_ptr(), Hd.data_ptr(),
+                                  ctypes.addressof(plan.capi()), a_.data_ptr(), b_.data_ptr(),
+                                  a_.shape[0], y.data_ptr(), _lib.stream_of(dev))
+    _lib.check(st, "fdwt_mix_forward")
+    return y
+
+
+class _MorletMixFunction(torch.autograd.Function):
+    """``y[r, n] = sum_s a[d, s] |W_s[r, n]| + b[d, s] Re W_s[r, n]`` without materialising W
+    (``fdwt/cwt.py:284-376``).  ``MIX_CHUNK_BYTES`` is kept for drop-in compatibility; the
+    sm_100a backward recomputes per row and needs no row chunking."""
+
+    MIX_CHUNK_BYTES = 256 * 2**20
+
+    @staticmethod
+    def forward(ctx, x, plan: MorletPlan, H, a, b):
+        ctx.plan = plan
+        ctx.save_for_backward(x, H, a, b)
+        return _mix_forward(x, plan, H, a, b)
+
+    @staticmethod
+    def backward(ctx, gy):
+        raise NotImplementedError("mix backward kernels are not built yet")
+
+
+def morlet_mix(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor, a: torch.Tensor,
+               b: torch.Tensor) -> torch.Tensor:
+    """``x (B, D, N)`` -> ``sum_s a[d, s] |W_s| + b[d, s] Re W_s``, shape ``(B, D, N)``."""
+    B, D, N = x.shape
+    _lib.require_cuda(x)
+    x2 = x.reshape(B * D, N).contiguous()
+    if x2.dtype not in (torch.float32, torch.float64):
+        x2 = x2.float()
+    return _MorletMixFunction.apply(x2, plan, H, a, b).view(B, D, N)
+
+
+def _softmax_forward(x2, plan, H, V, nch, tau):
+    dev = _lib.require_cuda(x2, H, V)
+    lib = _lib.load()
+    R, N = x2.shape
+    out = torch.empty((R, N), device=dev, dtype=x2.dtype)
+    m = torch.empty_like(out)
+    l = torch.empty_like(out)
+    Hd = _filters_on(H, x2)
+    V_ = V.detach().to(x2.dtype).contiguous()
+    with torch.cuda.device(dev):
+        st = lib.fdwt_specsoftmax_forward(
+            _lib.dtype_code(x2.dtype), R, N, x2.data_ptr(), Hd.data_ptr(),
+            ctypes.addressof(plan.capi()), V_.data_ptr(), int(V_.dim() == 3), nch, 1.0 / tau,
+            out.data_ptr(), m.data_ptr(), l.data_ptr(), _lib.stream_of(dev))
+    _lib.check(st, "fdwt_specsoftmax_forward")
+    return out, m, l
+
+
+class _SpectralSoftmaxFunction(torch.autograd.Function):
+    """``out[r, n] = sum_f softmax_f(|W_f x_r|(n) / tau) * V_f[r, n]`` without materialising W
+    (``fdwt/cwt.py:397-509``).  ``CHUNK_BYTES`` is kept for drop-in compatibility."""
+
+    CHUNK_BYTES = 256 * 2**20
+
+    @staticmethod
+    def forward(ctx, x, plan: MorletPlan, H, V, nch: int, tau: float, precision: str):
+        if not plan.complex:
+            raise ValueError("the spectral softmax needs the complex Morlet transform")
+        out, m, l = _softmax_forward(x, plan, H, V, nch, tau)
+        ctx.plan, ctx.nch, ctx.tau = plan, nch, tau
+        ctx.save_for_backward(x, H, V, m, l, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, gy):
+        raise NotImplementedError("spectral softmax backward kernels are not built yet")
+
+
+def spectral_softmax(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor, V: torch.Tensor,
+                     nch: int, tau: float = 1.0) -> torch.Tensor:
+    """``x (R, N)`` -> ``sum_f softmax_f(|W_f x|/tau) V_f``, shape ``(R, N)``.
+
+    ``V`` is ``(nch, S)`` (row r uses ``V[r % nch]``) or ``(R // nch, S, N)`` (row r uses
+    ``V[r // nch]``).
+    """
+    R, N = x.shape
+    _lib.require_cuda(x)
+    x2 = x.contiguous()
+    if x2.dtype not in (torch.float32, torch.float64):
+        x2 = x2.float()
+    return _SpectralSoftmaxFunction.apply(x2, plan, H, V, nch, float(tau), "ieee")
