@@ -40,7 +40,8 @@ enum {
   FDWT_ERR_INVALID = 1,     /* bad argument: null pointer, negative or inconsistent size  */
   FDWT_ERR_UNSUPPORTED = 2, /* valid but outside what the kernels implement (e.g. L > 64)  */
   FDWT_ERR_WORKSPACE = 3,   /* workspace missing or smaller than the matching *_workspace() */
-  FDWT_ERR_CUDA = 4         /* a CUDA runtime call failed; see fdwt_last_cuda_error()      */
+  FDWT_ERR_CUDA = 4,        /* a CUDA runtime call failed; see fdwt_last_cuda_error()      */
+  FDWT_ERR_SCRATCH_LIMIT = 5 /* the call needs more than FDWT_NOALLOC_SCRATCH_BYTES        */
 };
 
 /* Human-readable name of a status code (static storage). */
@@ -103,6 +104,31 @@ int fdwt_dwt_synthesis(int dtype, int64_t rows, int levels, const void* const* i
 size_t fdwt_dwt_synthesis_workspace(int dtype, int64_t rows, int levels, int64_t approx_len,
                                     const int64_t* coef_len, const int64_t* out_len,
                                     int filter_len, int mode, int off);
+
+/* Size of the static device array behind fdwt_dwt_analysis_noalloc (16 MiB). */
+#define FDWT_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+
+/* fdwt_dwt_analysis for callers that cannot allocate device memory while they run (a real-time
+ * loop where cudaMalloc/cudaFree would synchronise the device, or a host whose own allocator
+ * owns the GPU and cannot pass a workspace through its FFI).  No counterpart in the reference:
+ * it has no C interface and allocates through torch.
+ *
+ * Same arguments and results as fdwt_dwt_analysis without the workspace pair.  The workspace
+ * that long rows need is a file-scope device array of FDWT_NOALLOC_SCRATCH_BYTES compiled into
+ * the library; every GPU that loads the library holds it until the process exits.  The call
+ * allocates nothing.
+ *  - Sizes whose fdwt_dwt_analysis_workspace() exceeds FDWT_NOALLOC_SCRATCH_BYTES return
+ *    FDWT_ERR_SCRATCH_LIMIT without launching anything.
+ *  - The first call on a device that needs the array (multi-launch rows) looks up the array's
+ *    device address with that device current (cudaGetSymbolAddress) and caches it; make that
+ *    first call before any stream capture.
+ *  - Every call on a device shares the one array and leaves its contents behind.  Nothing in it
+ *    needs to start at zero, but calls that overlap on the GPU (different streams, or different
+ *    host threads, without ordering between them) race on it: serialise them. */
+int fdwt_dwt_analysis_noalloc(int dtype, int64_t rows, const void* x, int64_t n, int levels,
+                              const int64_t* coef_len, const int64_t* pad_last, void* const* out,
+                              const double* h0, const double* h1, int filter_len, int mode,
+                              int off, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Morlet continuous wavelet transform (the a-trous octave pyramid of MorletPlan).

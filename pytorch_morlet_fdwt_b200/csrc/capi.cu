@@ -64,6 +64,8 @@ extern "C" const char* fdwt_status_string(int status) {
     case FDWT_ERR_UNSUPPORTED: return "unsupported configuration";
     case FDWT_ERR_WORKSPACE: return "workspace missing or too small";
     case FDWT_ERR_CUDA: return "CUDA runtime error";
+    case FDWT_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the static no-allocation array holds";
     default: return "unknown status";
   }
 }

@@ -1,5 +1,7 @@
 // C ABI of the fused multilevel DWT (kernels in dwt_impl.cuh, instantiated per dtype in
 // dwt_f32.cu / dwt_f64.cu / dwt_f16.cu / dwt_bf16.cu).
+#include <mutex>
+
 #include "dwt_impl.cuh"
 
 namespace fdwt {
@@ -146,4 +148,69 @@ extern "C" size_t fdwt_dwt_synthesis_workspace(int dtype, int64_t rows, int leve
                    static_cast<void*>(nullptr), size_t(0), static_cast<cudaStream_t>(nullptr),
                    &need);
   return need;
+}
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free analysis.  Some callers cannot allocate device memory once they are running:
+// a real-time acquisition loop where cudaMalloc/cudaFree would synchronise the device and stall
+// its other streams, or a host application whose own allocator owns the device and whose FFI
+// has no way to hand this library a workspace buffer.  fdwt_dwt_analysis_noalloc serves them:
+// the workspace that long rows need (the approximation handed from one launch to the next) is
+// a fixed array compiled into this file, which every GPU that loads the library holds until
+// the process exits.
+// ------------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // FDWT_NOALLOC_SCRATCH_BYTES
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device.  In host code the array's name is
+// only a host-side stand-in, so the address comes from cudaGetSymbolAddress, looked up once per
+// device with that device current (the first call on each device) and cached.
+int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[kNoAllocMaxDevices] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    fdwt::set_cuda_error(e);
+    return FDWT_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return FDWT_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      fdwt::set_cuda_error(e);
+      return FDWT_ERR_CUDA;
+    }
+    if (p == nullptr) return FDWT_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return FDWT_OK;
+}
+
+}  // namespace
+
+extern "C" int fdwt_dwt_analysis_noalloc(int dtype, int64_t rows, const void* x, int64_t n,
+                                         int levels, const int64_t* coef_len,
+                                         const int64_t* pad_last, void* const* out,
+                                         const double* h0, const double* h1, int filter_len,
+                                         int mode, int off, void* stream) {
+  const size_t need = fdwt_dwt_analysis_workspace(dtype, rows, n, levels, coef_len, pad_last,
+                                                  filter_len, mode, off);
+  if (need > kNoAllocScratchBytes) return FDWT_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int st = noalloc_scratch(&scratch);
+    if (st != FDWT_OK) return st;
+  }
+  // Every element of a handover region is written by one launch before the next launch reads
+  // it, so nothing left in the array by an earlier call needs clearing.
+  return fdwt_dwt_analysis(dtype, rows, x, n, levels, coef_len, pad_last, out, h0, h1,
+                           filter_len, mode, off, scratch, need, stream);
 }
