@@ -138,8 +138,9 @@ int fdwt_dwt_analysis_noalloc(int dtype, int64_t rows, const void* x, int64_t n,
  * scale indices, sorted by support) whose filters have 2*oct_half[j]+1 taps at spacing 2^j;
  * x_j (j >= 1) is the dilated half-band low-pass of x_{j-1} materialised on
  * [-margins[j], n + margins[j]).  Filters are the (n_scales*channels, 2*center+1) tensor of
- * MorletPlan.filters (row i*channels + c), read from device memory; scale i uses taps
- * center-support[i] .. center+support[i] (the rest are zero by construction).
+ * MorletPlan.filters (row i*channels + c), read from device memory; every scale of octave j
+ * uses the taps center-oct_half[j] .. center+oct_half[j], as the reference's CPU path does
+ * (MorletPlan.filters makes the taps past a scale's support zero).
  * ---------------------------------------------------------------------------------------- */
 #define FDWT_MAX_OCTAVES 24
 #define FDWT_MAX_SCALES 256
@@ -183,6 +184,48 @@ int fdwt_specsoftmax_forward(int dtype, int64_t rows, int64_t n, const void* x,
                              const void* filters, const fdwt_morlet_plan* plan, const void* v,
                              int v_per_position, int64_t nch, double inv_tau, void* out, void* m,
                              void* l, void* stream);
+
+/* Backward passes.  One kernel per call runs a row's whole adjoint chain (coarsest octave
+ * first) and, when requested, the filter gradient; per-row partial sums are then reduced over
+ * rows in a fixed order, so results are deterministic (except dL/dV of a per-position V, which
+ * is accumulated with atomic adds).  Gradients are in the computation type (fp32 or fp64).
+ * Null output pointers skip that output.  The workspace holds the rebuilt pyramid and the
+ * per-row partials; query its size with the matching *_workspace function (need_gh says
+ * whether gh will be requested). */
+
+/* dL/dx (rows, n) and dL/dH (n_scales*channels, 2*center+1) from dL/dW (rows, n_scales, n,
+ * channels).  x is only read when gh is requested.  Replaces backward_x, backward_h and the
+ * transposed half-band (fdwt/kernels/conv.py:345-430) as issued by
+ * _MorletCWTFunction.backward (fdwt/cwt.py:246-281). */
+size_t fdwt_cwt_backward_workspace(int dtype, int64_t rows, int64_t n,
+                                   const fdwt_morlet_plan* plan, int need_gh);
+int fdwt_cwt_backward(int dtype, int64_t rows, int64_t n, const void* x, const void* filters,
+                      const fdwt_morlet_plan* plan, const void* gy, void* gx, void* gh,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward of fdwt_mix_forward from dL/dy (rows, n): dL/dx, dL/dH, dL/da and dL/db (dim,
+ * n_scales).  W is recomputed, never stored.  Replaces mix_backward (fdwt/kernels/mix.py:92-108)
+ * and the backward_x / backward_h calls of _MorletMixFunction.backward (fdwt/cwt.py:322-376). */
+size_t fdwt_mix_backward_workspace(int dtype, int64_t rows, int64_t n,
+                                   const fdwt_morlet_plan* plan, int64_t dim, int need_gh);
+int fdwt_mix_backward(int dtype, int64_t rows, int64_t n, const void* x, const void* filters,
+                      const fdwt_morlet_plan* plan, const void* a, const void* b, int64_t dim,
+                      const void* gy, void* gx, void* gh, void* ga, void* gb, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Backward of fdwt_specsoftmax_forward from dL/dout (rows, n), given the forward's out, m and
+ * l: dL/dx, dL/dH and dL/dV (the shape of V).  Replaces backward_stage
+ * (fdwt/kernels/softmax.py:206-210) and the octave loop of _SpectralSoftmaxFunction.backward
+ * (fdwt/cwt.py:452-509). */
+size_t fdwt_specsoftmax_backward_workspace(int dtype, int64_t rows, int64_t n,
+                                           const fdwt_morlet_plan* plan, int v_per_position,
+                                           int64_t nch, int need_gh);
+int fdwt_specsoftmax_backward(int dtype, int64_t rows, int64_t n, const void* x,
+                              const void* filters, const fdwt_morlet_plan* plan, const void* v,
+                              int v_per_position, int64_t nch, double inv_tau, const void* m,
+                              const void* l, const void* out, const void* gout, void* gx,
+                              void* gh, void* gv, void* workspace, size_t workspace_bytes,
+                              void* stream);
 
 #ifdef __cplusplus
 }

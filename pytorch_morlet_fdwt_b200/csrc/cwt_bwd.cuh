@@ -1,0 +1,745 @@
+// Backward of the Morlet CWT pyramid for sm_100a: the adjoint of the transform (dL/dx), the
+// filter gradient (dL/dH) and the fused epilogues of the two scalogram consumers (mix and
+// spectral softmax), which recompute W instead of storing it.  Included by cwt.cu after
+// cwt_impl.cuh.
+//
+// One CTA owns one row.  The forward pyramid is x_{j+1} = LP_j x_j and W_j = M_j x_j, so
+//   dL/dx_j = M_j^T dL/dW_j + LP_j^T dL/dx_{j+1},
+// a chain that runs from the coarsest octave to the finest (fdwt/cwt.py:248-281), while the
+// filter gradient of octave j needs x_j, which is built from the finest octave up.  The kernel
+// therefore runs two passes over a row:
+//   1. fine -> coarse: rebuild x_1 .. x_{J-1} (the half-band chain of the forward) and store
+//      each on its live extent in a per-row global scratch (only when a pass-2 consumer needs
+//      x_j: the filter gradient, or the recomputation of W for mix / softmax);
+//   2. coarse -> fine: G_j = LP_j^T G_{j+1}; then, scale by scale, stage dL/dW_s in shared
+//      memory (read from the caller, or formed from the recomputed W_s and the epilogue's
+//      saved state), add M_s^T dL/dW_s into G_j, and reduce dL/dH_s = sum_n dL/dW_s(n) x_j(n-dk)
+//      into a per-row partial.  dL/dx = G_0.
+// x_j is zero outside [-live_j, n + live_j) (live_j as in the forward), and so is any gradient
+// that can reach x_0 through it: every shared buffer covers [-E, n + E) with E = max live + 1,
+// reads are clamped into that range, and the two end cells are always zero.
+//
+// Reductions over rows (dL/dH, the mix weights, per-channel V) are written as per-row partials
+// and summed by reduce_rows_kernel in a fixed order, so results are deterministic.  The
+// per-position V gradient of the spectral softmax (V of shape (G, S, n), shared by the nch rows
+// of a group) is accumulated with atomic adds.
+#pragma once
+
+#include "cwt_impl.cuh"
+
+namespace fdwt {
+namespace cwtk {
+
+constexpr int NW = NT / 32;  // warps per CTA
+constexpr int KT = 8;        // taps per thread in the filter-gradient reduction
+
+template <typename A>
+struct BwdParams {
+  FwdParams<A> f;     // plan, filters f.h, input f.x, MIX a/b or SOFTMAX V in f.a/f.b, f.dim,
+                      // f.v_pos, f.inv_tau; f.ext = E (buffer reach), f.buf_len
+  const A* g;         // STORE: dL/dW (rows, S, n, C); MIX: dL/dy (rows, n); SOFTMAX: dL/dout
+  const A* sm_m;      // SOFTMAX saved state (rows, n): running max, denominator, output
+  const A* sm_l;
+  const A* sm_out;
+  A* gx;              // (rows, n) or null
+  A* gh_part;         // (rows, S*C*hcols) per-row filter gradient or null
+  A* a_part;          // MIX: (rows, S) partials of dL/da and dL/db
+  A* b_part;
+  A* v_part;          // SOFTMAX: per-channel V: (rows, S) partials; per-position V: dL/dV (G, S, n)
+  A* pyr;             // (rows, pyr_len) pyramid scratch or null
+  int64_t pyr_len;
+  int32_t pyr_off[kMaxOct];  // start of x_j in a row's scratch (-1: not stored)
+  int32_t need_gx;    // build G (dL/dx) at all
+  int32_t need_x;     // pass 2 reads x_j (filter gradient, or recomputation of W)
+  int32_t gw_len;     // elements of the dL/dW buffer
+  int32_t gw_off, tab_off, red_off;  // byte offsets of the dL/dW buffer, tap table, reduce slots
+};
+
+template <typename A>
+struct Cplx;
+template <>
+struct Cplx<float> {
+  using type = float2;
+};
+template <>
+struct Cplx<double> {
+  using type = double2;
+};
+
+// ------------------------------------------------------------------------------ buffers
+
+template <typename A>
+__device__ __forceinline__ int clampE(const FwdParams<A>& f, int pos) {
+  return min(max(pos, -f.ext), static_cast<int>(f.n) + f.ext - 1);
+}
+template <typename A>
+__device__ __forceinline__ A ldE(const FwdParams<A>& f, const A* buf, int pos) {
+  return buf[sidx<PS>(clampE(f, pos) + f.ext)];
+}
+template <typename A>
+__device__ __forceinline__ A& atE(const FwdParams<A>& f, A* buf, int pos) {
+  return buf[sidx<PS>(pos + f.ext)];
+}
+
+// dL/dW buffer: positions [-1, n] (the two ends stay zero), complex values interleaved.
+template <typename A, int C>
+__device__ __forceinline__ typename Cplx<A>::type ld_gw(const A* gw, int n, int pos) {
+  const int q = sidx<PS>(min(max(pos, -1), n) + 1);
+  typename Cplx<A>::type v;
+  if (C == 2) {
+    v = *reinterpret_cast<const typename Cplx<A>::type*>(gw + 2 * q);
+  } else {
+    v.x = gw[q];
+    v.y = A(0);
+  }
+  return v;
+}
+template <typename A, int C>
+__device__ __forceinline__ void st_gw(A* gw, int pos, A re, A im) {
+  const int q = sidx<PS>(pos + 1);
+  if (C == 2) {
+    gw[2 * q] = re;
+    gw[2 * q + 1] = im;
+  } else {
+    gw[q] = re;
+  }
+}
+
+// Deterministic CTA sum of one value per thread (all threads must call it).
+template <typename A>
+__device__ __forceinline__ A block_sum(A v, A* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  A s = A(0);
+  if (threadIdx.x == 0)
+    for (int i = 0; i < NW; ++i) s += red[i];
+  return s;  // valid in thread 0
+}
+
+// Folded taps of one scale (k = 0..K), as in the forward's coefficient table; returns whether
+// the antisymmetric-real / symmetric-imaginary halves are all zero (exactly symmetric filter).
+template <typename A>
+__device__ bool build_scale_taps(const FwdParams<A>& f, const Oct& O, int s, A* tab, int* flag) {
+  if (threadIdx.x == 0) *flag = 0;
+  __syncthreads();
+  for (int k = threadIdx.x; k <= O.half; k += NT) {
+    A t[4];
+    fold_coef<A>(f, O, s, k, t);
+    tab[4 * k + 0] = t[0];
+    tab[4 * k + 1] = t[1];
+    tab[4 * k + 2] = t[2];
+    tab[4 * k + 3] = t[3];
+    if (t[2] != A(0) || t[3] != A(0)) atomicOr(flag, 1);
+  }
+  __syncthreads();
+  return *flag == 0;
+}
+
+// ------------------------------------------------------------------------------ pyramid
+
+// x_{j+1} = LP_j x_j on the whole buffer (zero outside live_{j+1}), reads clamped.
+template <typename A>
+__device__ void bwd_lowpass(const FwdParams<A>& f, const A* cur, A* nxt, int dil, int live) {
+  const int n = static_cast<int>(f.n);
+  for (int q = static_cast<int>(threadIdx.x) - f.ext; q < n + f.ext; q += NT) {
+    A v = A(0);
+    if (q >= -live && q < n + live) {
+      v = f.lpp[0] * ldE(f, cur, q);
+      for (int t = 1; t <= f.c_lp; ++t) {
+        v = fma(f.lpp[t], ldE(f, cur, q - dil * t), v);
+        v = fma(f.lpm[t], ldE(f, cur, q + dil * t), v);
+      }
+    }
+    atE(f, nxt, q) = v;
+  }
+}
+
+// G_j = LP_j^T G_{j+1} on the whole buffer (zero outside live_j):
+//   G_j(p) = lpp[0] G(p) + sum_t lpp[t] G(p + dil t) + lpm[t] G(p - dil t).
+template <typename A>
+__device__ void bwd_lowpass_adjoint(const FwdParams<A>& f, const A* src, A* dst, int dil,
+                                    int live) {
+  const int n = static_cast<int>(f.n);
+  for (int q = static_cast<int>(threadIdx.x) - f.ext; q < n + f.ext; q += NT) {
+    A v = A(0);
+    if (q >= -live && q < n + live) {
+      v = f.lpp[0] * ldE(f, src, q);
+      for (int t = 1; t <= f.c_lp; ++t) {
+        v = fma(f.lpp[t], ldE(f, src, q + dil * t), v);
+        v = fma(f.lpm[t], ldE(f, src, q - dil * t), v);
+      }
+    }
+    atE(f, dst, q) = v;
+  }
+}
+
+// ------------------------------------------------------------------------------ per scale
+
+// (re, im) of one scale at the P outputs n_i = base + dil i, windows read from X (clamped).
+template <typename A, bool SYM>
+__device__ __forceinline__ void conv_one(const FwdParams<A>& f, const A* X, const A* tab, int K,
+                                         int dil, int base, Acc2<A> (&acc)[P]) {
+  A L[P], R[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) L[i] = R[i] = ldE(f, X, base + dil * i);
+  {
+    alignas(16) A t0[2] = {tab[0], tab[3]};
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      acc[i].zero();
+      acc[i].fma(t0, L[i], L[i]);
+    }
+  }
+  int pl = base - dil, pr = base + dil * P;
+  for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
+#pragma unroll
+    for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
+#pragma unroll
+    for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
+    L[0] = ldE(f, X, pl);
+    R[P - 1] = ldE(f, X, pr);
+    alignas(16) A t[4] = {tab[4 * k], tab[4 * k + 1], tab[4 * k + 2], tab[4 * k + 3]};
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const A sum = L[i] + R[i], dif = L[i] - R[i];
+      acc[i].fma(t, sum, dif);
+      if (!SYM) acc[i].fma(t + 2, dif, sum);
+    }
+  }
+}
+
+// G(p) += sum_k h_re(k) gWre(p + dk) + h_im(k) gWim(p + dk) for p in [pa, pb).
+template <typename A, int C, bool SYM>
+__device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab, const A* gw,
+                              A* G, int pa, int pb) {
+  const int n = static_cast<int>(f.n);
+  const int dil = O.dil, K = O.half;
+  const int len = pb - pa;
+  if (len <= 0) return;
+  const int runs = static_cast<int>(cdiv(cdiv(len, dil), P));
+  const int items = dil * runs;
+  using V2 = typename Cplx<A>::type;
+  for (int it = threadIdx.x; it < items; it += NT) {
+    const int phi = it % dil, u0 = (it / dil) * P;
+    if (phi >= len) continue;
+    const int base = pa + phi + dil * u0;
+    V2 L[P], R[P];
+    Acc2<A> acc[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) L[i] = R[i] = ld_gw<A, C>(gw, n, base + dil * i);
+    {
+      alignas(16) A t0[2] = {tab[0], tab[3]};
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        acc[i].zero();
+        acc[i].fma(t0, L[i].x, L[i].y);
+      }
+    }
+    int pl = base - dil, pr = base + dil * P;
+    for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
+#pragma unroll
+      for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
+#pragma unroll
+      for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
+      L[0] = ld_gw<A, C>(gw, n, pl);
+      R[P - 1] = ld_gw<A, C>(gw, n, pr);
+      alignas(16) A t[4] = {tab[4 * k], tab[4 * k + 1], tab[4 * k + 2], tab[4 * k + 3]};
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        acc[i].fma(t, R[i].x + L[i].x, R[i].y - L[i].y);
+        if (!SYM) acc[i].fma(t + 2, R[i].x - L[i].x, R[i].y + L[i].y);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const int q = base + dil * i;
+      if (q < pb) atE(f, G, q) += acc[i].re() + acc[i].im();
+    }
+  }
+}
+
+// Per-row dL/dH of one scale: part[c*hcols + center + k] = sum_n gW_c(n) x_j(n - dil k) for
+// |k| <= K (zero elsewhere).  Warp w reduces taps [k0, k0 + KT) for kb = w, w + NW, ...; its
+// lanes split the positions (in phase-major order, so a window slides by one tap per step)
+// and are summed with shuffles.
+template <typename A, int C>
+__device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, const A* gw,
+                            A* part) {
+  const int n = static_cast<int>(f.n);
+  const int dil = O.dil, K = O.half;
+  const int hcols = 2 * f.center + 1;
+  const int ntap = 2 * K + 1;
+  const int nkb = static_cast<int>(cdiv(ntap, KT));
+  const int U = static_cast<int>(cdiv(n, dil));
+  const int tot = dil * U;
+  const int T = static_cast<int>(cdiv(tot, 32));
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  using V2 = typename Cplx<A>::type;
+  for (int c = threadIdx.x; c < C * hcols; c += NT) {
+    const int k = c % hcols - f.center;
+    if (k < -K || k > K) part[c] = A(0);
+  }
+  for (int kb = w; kb < nkb; kb += NW) {
+    const int k0 = -K + kb * KT;
+    Acc2<A> acc[KT];
+#pragma unroll
+    for (int i = 0; i < KT; ++i) acc[i].zero();
+    const int i0 = lane * T, i1 = min(tot, i0 + T);
+    if (i0 < i1) {
+      int phi = i0 / U, u = i0 - phi * U;
+      A win[KT];
+      bool fresh = true;
+      for (int idx = i0; idx < i1; ++idx) {
+        const int nn = phi + dil * u;
+        if (nn < n) {
+          if (fresh) {
+#pragma unroll
+            for (int i = 0; i < KT; ++i) win[i] = ldE(f, X, nn - dil * (k0 + i));
+            fresh = false;
+          } else {
+#pragma unroll
+            for (int i = KT - 1; i > 0; --i) win[i] = win[i - 1];
+            win[0] = ldE(f, X, nn - dil * k0);
+          }
+          const V2 gv = ld_gw<A, C>(gw, n, nn);
+          alignas(16) A gp[2] = {gv.x, gv.y};
+#pragma unroll
+          for (int i = 0; i < KT; ++i) acc[i].fma(gp, win[i], win[i]);
+        }
+        if (++u == U) {
+          u = 0;
+          ++phi;
+          fresh = true;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < KT; ++i) {
+      A re = acc[i].re(), im = acc[i].im();
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        re += __shfl_xor_sync(0xffffffffu, re, o);
+        if (C == 2) im += __shfl_xor_sync(0xffffffffu, im, o);
+      }
+      const int k = k0 + i;
+      if (lane == 0 && k <= K) {
+        part[f.center + k] = re;
+        if (C == 2) part[hcols + f.center + k] = im;
+      }
+    }
+  }
+}
+
+// dL/dW_s on [0, n) into the gW buffer.  STORE: copied from the caller's gradient.  MIX /
+// SOFTMAX: W_s is recomputed from x_j and the epilogue's derivative applied; the per-row
+// parameter partials are returned through *pa_sum, *pb_sum (thread-local, summed by caller).
+template <typename A, int EPI, int C, bool SYM>
+__device__ void make_gw(const BwdParams<A>& p, const Oct& O, int s, int gs, const A* X,
+                        const A* tab, A* gw, int64_t row, A& sa, A& sb) {
+  const FwdParams<A>& f = p.f;
+  const int n = static_cast<int>(f.n);
+  if (EPI == EPI_STORE) {
+    const A* g = p.g + (row * f.n_scales + gs) * f.n * C;
+    for (int q = threadIdx.x; q < n; q += NT) {
+      if (C == 2) {
+        const typename Cplx<A>::type v = reinterpret_cast<const typename Cplx<A>::type*>(g)[q];
+        st_gw<A, C>(gw, q, v.x, v.y);
+      } else {
+        st_gw<A, C>(gw, q, g[q], A(0));
+      }
+    }
+    return;
+  }
+  const int dil = O.dil;
+  const int runs = static_cast<int>(cdiv(cdiv(n, dil), P));
+  const int items = dil * runs;
+  const A* gy = p.g + row * f.n;
+  A av = A(0), bv = A(0), vconst = A(0);
+  int64_t grp = 0;
+  if (EPI == EPI_MIX) {
+    const int64_t d = row % f.dim;
+    av = static_cast<const A*>(f.a)[d * f.n_scales + gs];
+    bv = static_cast<const A*>(f.b)[d * f.n_scales + gs];
+  } else {
+    grp = row / f.dim;
+    if (!f.v_pos) vconst = static_cast<const A*>(f.a)[(row % f.dim) * f.n_scales + gs];
+  }
+  for (int it = threadIdx.x; it < items; it += NT) {
+    const int phi = it % dil, u0 = (it / dil) * P;
+    if (phi >= n) continue;
+    const int base = phi + dil * u0;
+    Acc2<A> acc[P];
+    conv_one<A, SYM>(f, X, tab, O.half, dil, base, acc);
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const int q = base + dil * i;
+      if (q >= n) continue;
+      const A re = acc[i].re(), im = C == 2 ? acc[i].im() : A(0);
+      const A mag = C == 2 ? sqrt(re * re + im * im) : fabs(re);
+      const A go = gy[q];
+      A gre, gim;
+      if (EPI == EPI_MIX) {
+        sa += go * mag;
+        sb += go * re;
+        if (C == 2) {
+          const A r = mag > A(0) ? av * go / mag : A(0);
+          gre = r * re + bv * go;
+          gim = r * im;
+        } else {
+          const A sg = re > A(0) ? A(1) : (re < A(0) ? A(-1) : A(0));
+          gre = go * (av * sg + bv);
+          gim = A(0);
+        }
+      } else {
+        const int64_t rq = row * f.n + q;
+        const A a = mag * f.inv_tau;
+        const A pr = exp(a - p.sm_m[rq]) / p.sm_l[rq];
+        const A v = f.v_pos ? static_cast<const A*>(f.a)[(grp * f.n_scales + gs) * f.n + q]
+                            : vconst;
+        const A gmag = pr * (v - p.sm_out[rq]) * go * f.inv_tau;
+        if (f.v_pos) atomicAdd(p.v_part + (grp * f.n_scales + gs) * f.n + q, pr * go);
+        else sa += pr * go;
+        const A r = mag > A(0) ? gmag / mag : A(0);
+        gre = r * re;
+        gim = r * im;
+      }
+      st_gw<A, C>(gw, q, gre, gim);
+    }
+  }
+}
+
+template <typename A, int EPI, int C, bool SYM>
+__device__ void scale_pass(const BwdParams<A>& p, const Oct& O, int live, int s, A* G,
+                           const A* X, A* gw, const A* tab, A* red, int64_t row) {
+  const FwdParams<A>& f = p.f;
+  const int gs = f.order[O.begin + s];
+  A sa = A(0), sb = A(0);
+  make_gw<A, EPI, C, SYM>(p, O, s, gs, X, tab, gw, row, sa, sb);
+  if (EPI == EPI_MIX) {
+    const A ta = block_sum(sa, red);
+    const A tb = block_sum(sb, red);
+    if (threadIdx.x == 0) {
+      p.a_part[row * f.n_scales + gs] = ta;
+      p.b_part[row * f.n_scales + gs] = tb;
+    }
+  } else if (EPI == EPI_SOFTMAX && !f.v_pos) {
+    const A ta = block_sum(sa, red);
+    if (threadIdx.x == 0) p.v_part[row * f.n_scales + gs] = ta;
+  }
+  __syncthreads();
+  if (p.need_gx) {
+    const int reach = min(live, O.half * O.dil);
+    adjoint_scale<A, C, SYM>(f, O, tab, gw, G, -reach, static_cast<int>(f.n) + reach);
+  }
+  if (p.gh_part) {
+    const int hcols = 2 * f.center + 1;
+    gradh_scale<A, C>(f, O, X, gw, p.gh_part + (row * f.n_scales + gs) * C * hcols);
+  }
+  __syncthreads();
+}
+
+template <typename A, int EPI, int C>
+__device__ void octave_pass(const BwdParams<A>& p, const Oct& O, int live, A* G, const A* X,
+                            A* gw, A* tab, int* flag, A* red, int64_t row) {
+  for (int s = 0; s < O.count; ++s) {
+    const bool sym = build_scale_taps<A>(p.f, O, s, tab, flag);
+    if (sym) scale_pass<A, EPI, C, true>(p, O, live, s, G, X, gw, tab, red, row);
+    else scale_pass<A, EPI, C, false>(p, O, live, s, G, X, gw, tab, red, row);
+  }
+}
+
+template <typename A, int EPI>
+__global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant__ BwdParams<A> p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const FwdParams<A>& f = p.f;
+  A* bufs[3] = {reinterpret_cast<A*>(smem), reinterpret_cast<A*>(smem) + f.buf_len,
+                reinterpret_cast<A*>(smem) + 2 * f.buf_len};
+  A* gw = reinterpret_cast<A*>(smem + p.gw_off);
+  A* tab = reinterpret_cast<A*>(smem + p.tab_off);
+  A* red = reinterpret_cast<A*>(smem + p.red_off);
+  __shared__ int flag;
+  const int64_t row = blockIdx.x;
+  const int n = static_cast<int>(f.n);
+  const int E = f.ext;
+  const int J = f.n_oct;
+  const A* xr = static_cast<const A*>(f.x) + row * f.n;
+
+  // the end cells of the dL/dW buffer (positions -1 and n) are never written again
+  for (int q = threadIdx.x; q < p.gw_len; q += NT) gw[q] = A(0);
+
+  // pass 1: x_1 .. x_{J-1} into the row's scratch
+  if (p.need_x && J > 1) {
+    A* cur = bufs[0];
+    A* nxt = bufs[1];
+    for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += NT)
+      atE(f, cur, q) = (q >= 0 && q < n) ? xr[q] : A(0);
+    __syncthreads();
+    for (int j = 0; j + 1 < J; ++j) {
+      bwd_lowpass<A>(f, cur, nxt, f.oct[j].dil, f.oct[j + 1].live);
+      __syncthreads();
+      if (p.pyr_off[j + 1] >= 0) {
+        const int lv = f.oct[j + 1].live;
+        A* dst = p.pyr + row * p.pyr_len + p.pyr_off[j + 1];
+        for (int q = static_cast<int>(threadIdx.x) - lv; q < n + lv; q += NT)
+          dst[q + lv] = atE(f, nxt, q);
+      }
+      A* t = cur;
+      cur = nxt;
+      nxt = t;
+    }
+    __syncthreads();
+  }
+
+  // pass 2: coarse -> fine
+  A* G = bufs[0];
+  A* Gn = bufs[1];
+  A* X = bufs[2];
+  for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += NT) atE(f, G, q) = A(0);
+  for (int j = J - 1; j >= 0; --j) {
+    const Oct& O = f.oct[j];
+    if (j + 1 < J && p.need_gx) {
+      __syncthreads();
+      bwd_lowpass_adjoint<A>(f, G, Gn, O.dil, O.live);
+      A* t = G;
+      G = Gn;
+      Gn = t;
+    }
+    if (O.count > 0) {
+      if (p.need_x) {
+        const int lv = O.live;
+        const A* srcp = j == 0 ? xr : p.pyr + row * p.pyr_len + p.pyr_off[j];
+        for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += NT)
+          atE(f, X, q) = (q >= -lv && q < n + lv) ? srcp[q + lv] : A(0);
+      }
+      __syncthreads();
+      if (f.channels == 2) octave_pass<A, EPI, 2>(p, O, O.live, G, X, gw, tab, &flag, red, row);
+      else octave_pass<A, EPI, 1>(p, O, O.live, G, X, gw, tab, &flag, red, row);
+    }
+  }
+  __syncthreads();
+  if (p.need_gx) {
+    A* gx = p.gx + row * f.n;
+    for (int q = threadIdx.x; q < n; q += NT) gx[q] = atE(f, G, q);
+  }
+}
+
+// out[d, e] = sum_{i} part[(d + i D), e] over the rows r = d + i D < rows, in order of i.
+// Two stages for parallelism: stage 1 sums row chunks into tmp, stage 2 sums the chunks.
+template <typename A>
+__global__ void reduce_rows_kernel(const A* __restrict__ part, int64_t rows, int64_t cols,
+                                   int64_t D, int64_t per_chunk, int64_t nchunk, A* __restrict__ out) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t d = blockIdx.y;
+  const int64_t ch = blockIdx.z;
+  if (e >= cols) return;
+  const int64_t per_d = cdiv(rows - d, D);  // rows of residue d
+  const int64_t i0 = ch * per_chunk, i1 = imin(per_d, i0 + per_chunk);
+  A s = A(0);
+  for (int64_t i = i0; i < i1; ++i) s += part[(d + i * D) * cols + e];
+  out[(ch * D + d) * cols + e] = s;
+}
+
+// ------------------------------------------------------------------------------ host
+
+// Two-stage reduction plan of reduce_rows: chunks per residue so that stage 1 fills the GPU.
+inline int64_t reduce_chunks(int64_t rows, int64_t cols, int64_t D) {
+  const int64_t per_d = cdiv(rows, D);
+  const int64_t blocks = cdiv(cols, 256) * D;
+  int64_t nch = cdiv(2 * static_cast<int64_t>(sm_count()), blocks);
+  nch = imin(nch, imax(1, per_d / 16));
+  return imax(1, nch);
+}
+inline size_t reduce_tmp_elems(int64_t rows, int64_t cols, int64_t D) {
+  const int64_t nch = reduce_chunks(rows, cols, D);
+  return nch > 1 ? static_cast<size_t>(nch * D * cols) : 0;
+}
+
+template <typename A>
+int reduce_rows(const A* part, int64_t rows, int64_t cols, int64_t D, A* out, A* tmp,
+                cudaStream_t stream) {
+  if (cols == 0 || D == 0) return FDWT_OK;
+  if (D > 65535) return FDWT_ERR_UNSUPPORTED;
+  const int64_t nch = reduce_chunks(rows, cols, D);
+  const int64_t per_d = cdiv(rows, D);
+  const dim3 block(256);
+  if (nch == 1) {
+    reduce_rows_kernel<A><<<dim3(static_cast<unsigned>(cdiv(cols, 256)), static_cast<unsigned>(D), 1),
+                            block, 0, stream>>>(part, rows, cols, D, per_d, 1, out);
+    return launch_status();
+  }
+  const int64_t per_chunk = cdiv(per_d, nch);
+  reduce_rows_kernel<A><<<dim3(static_cast<unsigned>(cdiv(cols, 256)), static_cast<unsigned>(D),
+                               static_cast<unsigned>(nch)),
+                          block, 0, stream>>>(part, rows, cols, D, per_chunk, nch, tmp);
+  int st = launch_status();
+  if (st != FDWT_OK) return st;
+  reduce_rows_kernel<A><<<dim3(static_cast<unsigned>(cdiv(cols, 256)), static_cast<unsigned>(D), 1),
+                          block, 0, stream>>>(tmp, nch * D, cols, D, nch, 1, out);
+  return launch_status();
+}
+
+// Workspace regions of one backward call (bytes, each 256-aligned).
+struct BwdLayout {
+  int64_t pyr_len = 0;
+  int32_t pyr_off[kMaxOct];
+  size_t pyr = 0, gh = 0, pa = 0, pb = 0, pv = 0, tmp = 0, total = 0;
+};
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+template <typename A>
+BwdLayout bwd_layout(int EPI, int64_t rows, int64_t n, const fdwt_morlet_plan* pl,
+                     const Geometry& g, bool need_h, int64_t dim, bool v_pos) {
+  BwdLayout L;
+  const int J = pl->n_octaves;
+  const bool need_x = need_h || EPI != EPI_STORE;
+  for (int j = 0; j < kMaxOct; ++j) L.pyr_off[j] = -1;
+  if (need_x)
+    for (int j = 1; j < J; ++j)
+      if (pl->oct_count[j] > 0) {
+        L.pyr_off[j] = static_cast<int32_t>(L.pyr_len);
+        L.pyr_len += n + 2 * static_cast<int64_t>(g.live[j]);
+      }
+  const int64_t S = pl->n_scales;
+  const int64_t hcols = 2 * static_cast<int64_t>(pl->center) + 1;
+  const int64_t ghcols = S * pl->channels * hcols;
+  L.pyr = align256(static_cast<size_t>(rows) * L.pyr_len * sizeof(A));
+  L.gh = need_h ? align256(static_cast<size_t>(rows) * ghcols * sizeof(A)) : 0;
+  L.pa = EPI == EPI_MIX ? align256(static_cast<size_t>(rows) * S * sizeof(A)) : 0;
+  L.pb = L.pa;
+  L.pv = (EPI == EPI_SOFTMAX && !v_pos) ? align256(static_cast<size_t>(rows) * S * sizeof(A)) : 0;
+  size_t tmp = 0;
+  if (need_h) tmp = std::max(tmp, reduce_tmp_elems(rows, ghcols, 1));
+  if (EPI == EPI_MIX) tmp = std::max(tmp, reduce_tmp_elems(rows, S, dim));
+  if (EPI == EPI_SOFTMAX && !v_pos) tmp = std::max(tmp, reduce_tmp_elems(rows, S, dim));
+  L.tmp = align256(tmp * sizeof(A));
+  L.total = L.pyr + L.gh + L.pa + L.pb + L.pv + L.tmp;
+  return L;
+}
+
+// Backward of the transform (EPI_STORE), of the mix (EPI_MIX) or of the spectral softmax
+// (EPI_SOFTMAX).  Outputs gx (rows, n), gh (S*C, 2*center+1), ga/gb (dim, S), gv (nch, S) or
+// (G, S, n); null outputs are skipped.  ws_needed != null: only report the workspace size (for
+// a call with or without gh, as need_h says).
+template <typename A, int EPI>
+int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
+                 const fdwt_morlet_plan* pl, const void* a, const void* b, int64_t dim,
+                 int v_pos, double inv_tau, const void* g, const void* sm_m, const void* sm_l,
+                 const void* sm_out, void* gx, void* gh, void* ga, void* gb, void* gv, bool need_h,
+                 void* ws, size_t ws_bytes, cudaStream_t stream, size_t* ws_needed) {
+  int st = check_plan(pl, n);
+  if (st != FDWT_OK) return st;
+  if (EPI == EPI_SOFTMAX && pl->channels != 2) return FDWT_ERR_INVALID;
+  if (rows > 0x7fffffffLL || n > 0x3fffffffLL) return FDWT_ERR_UNSUPPORTED;
+  const Geometry geo = geometry(pl);
+  if (ws_needed == nullptr) need_h = gh != nullptr;
+  if (v_pos && (dim < 1 || rows % dim != 0)) return FDWT_ERR_INVALID;
+  const BwdLayout lay = bwd_layout<A>(EPI, rows, n, pl, geo, need_h, dim, v_pos != 0);
+  if (ws_needed) {
+    *ws_needed = lay.total;
+    return FDWT_OK;
+  }
+  const int64_t S = pl->n_scales;
+  const int64_t hcols = 2 * static_cast<int64_t>(pl->center) + 1;
+  const int64_t ghcols = S * pl->channels * hcols;
+  // outputs that are sums over rows start from zero when there are no rows
+  if (rows == 0 || EPI == EPI_SOFTMAX) {
+    auto zero = [&](void* ptr, size_t bytes) -> int {
+      if (ptr == nullptr || bytes == 0) return FDWT_OK;
+      cudaError_t e = cudaMemsetAsync(ptr, 0, bytes, stream);
+      if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return FDWT_ERR_CUDA;
+      }
+      return FDWT_OK;
+    };
+    if (rows == 0) {
+      if ((st = zero(gh, ghcols * sizeof(A))) != FDWT_OK) return st;
+      if (EPI == EPI_MIX) {
+        if ((st = zero(ga, dim * S * sizeof(A))) != FDWT_OK) return st;
+        if ((st = zero(gb, dim * S * sizeof(A))) != FDWT_OK) return st;
+      }
+      if (EPI == EPI_SOFTMAX && !v_pos && (st = zero(gv, dim * S * sizeof(A))) != FDWT_OK)
+        return st;
+      return FDWT_OK;
+    }
+    if (v_pos && (st = zero(gv, static_cast<size_t>(rows / dim) * S * n * sizeof(A))) != FDWT_OK)
+      return st;
+  }
+  if (lay.total > 0 && (ws == nullptr || ws_bytes < lay.total)) return FDWT_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  A* pyr = reinterpret_cast<A*>(w);
+  A* ghp = reinterpret_cast<A*>(w + lay.pyr);
+  A* pa = reinterpret_cast<A*>(w + lay.pyr + lay.gh);
+  A* pb = reinterpret_cast<A*>(w + lay.pyr + lay.gh + lay.pa);
+  A* pv = reinterpret_cast<A*>(w + lay.pyr + lay.gh + lay.pa + lay.pb);
+  A* tmp = reinterpret_cast<A*>(w + lay.pyr + lay.gh + lay.pa + lay.pb + lay.pv);
+
+  BwdParams<A> p{};
+  fill_common(p.f, pl, geo, n);
+  int E = 0;
+  for (int j = 0; j < pl->n_octaves; ++j) E = std::max(E, geo.live[j]);
+  p.f.ext = E + 1;
+  p.f.rows = rows;
+  p.f.x = x;
+  p.f.h = h;
+  p.f.a = a;
+  p.f.b = b;
+  p.f.dim = dim;
+  p.f.v_pos = v_pos;
+  p.f.inv_tau = static_cast<A>(inv_tau);
+  p.f.buf_len = static_cast<int>(padded_len<PS>(n + 2 * static_cast<int64_t>(p.f.ext)) + 8);
+  p.g = static_cast<const A*>(g);
+  p.sm_m = static_cast<const A*>(sm_m);
+  p.sm_l = static_cast<const A*>(sm_l);
+  p.sm_out = static_cast<const A*>(sm_out);
+  p.gx = static_cast<A*>(gx);
+  p.gh_part = gh ? ghp : nullptr;
+  p.a_part = pa;
+  p.b_part = pb;
+  p.v_part = EPI == EPI_SOFTMAX ? (v_pos ? static_cast<A*>(gv) : pv) : nullptr;
+  p.pyr = lay.pyr_len > 0 ? pyr : nullptr;
+  p.pyr_len = lay.pyr_len;
+  for (int j = 0; j < kMaxOct; ++j) p.pyr_off[j] = lay.pyr_off[j];
+  p.need_gx = gx != nullptr;
+  p.need_x = (gh != nullptr || EPI != EPI_STORE) ? 1 : 0;
+  p.gw_len = static_cast<int>(2 * padded_len<PS>(n + 2) + 8);
+  size_t off = 3 * static_cast<size_t>(p.f.buf_len) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  p.gw_off = static_cast<int>(off);
+  off += static_cast<size_t>(p.gw_len) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  p.tab_off = static_cast<int>(off);
+  off += 4 * (static_cast<size_t>(pl->center) + 1) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  p.red_off = static_cast<int>(off);
+  off += NW * sizeof(A);
+  const size_t smem = off + 16;
+  const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
+  if (smem > budget) return FDWT_ERR_UNSUPPORTED;
+  if (!p.need_gx && gh == nullptr && EPI == EPI_STORE) return FDWT_OK;
+  auto kern = cwt_backward_kernel<A, EPI>;
+  st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
+  if (st != FDWT_OK) return st;
+  kern<<<static_cast<unsigned>(rows), NT, smem, stream>>>(p);
+  if ((st = launch_status()) != FDWT_OK) return st;
+  if (gh && (st = reduce_rows<A>(ghp, rows, ghcols, 1, static_cast<A*>(gh), tmp, stream)) != FDWT_OK)
+    return st;
+  if (EPI == EPI_MIX) {
+    if (ga && (st = reduce_rows<A>(pa, rows, S, dim, static_cast<A*>(ga), tmp, stream)) != FDWT_OK)
+      return st;
+    if (gb && (st = reduce_rows<A>(pb, rows, S, dim, static_cast<A*>(gb), tmp, stream)) != FDWT_OK)
+      return st;
+  }
+  if (EPI == EPI_SOFTMAX && !v_pos && gv &&
+      (st = reduce_rows<A>(pv, rows, S, dim, static_cast<A*>(gv), tmp, stream)) != FDWT_OK)
+    return st;
+  return FDWT_OK;
+}
+
+}  // namespace cwtk
+}  // namespace fdwt

@@ -132,9 +132,9 @@ __device__ __forceinline__ int block_size(int rem) {
 //   [2] anti(re) = (h_re[c+k] - h_re[c-k]) / 2   (k = 0: 0)
 //   [3] sym(im)  = (h_im[c+k] + h_im[c-k]) / 2   (k = 0: h_im[c])
 // so that  re += [0] (xl + xr) + [2] (xl - xr),  im += [1] (xl - xr) + [3] (xl + xr)  exactly
-// reproduces sum_k h[c+k] x[n - dk] over k = -sup..sup.  Taps beyond a scale's support are 0.
-// Returns (through flags[]) whether each block has nonzero [2]/[3] halves.
-// Folded coefficients of tap k of scale slot s, straight from the filter tensor.
+// reproduces sum_k h[c+k] x[n - dk] over k = -half..half of the octave.
+// build_coef returns (through flags[]) whether each block has nonzero [2]/[3] halves.
+// fold_coef: folded coefficients of tap k of scale slot s, straight from the filter tensor.
 template <typename A>
 __device__ __forceinline__ void fold_coef(const FwdParams<A>& p, const Oct& O, int s, int k,
                                           A (&t)[4]) {
@@ -142,16 +142,16 @@ __device__ __forceinline__ void fold_coef(const FwdParams<A>& p, const Oct& O, i
   const int C = p.channels;
   const int hcols = 2 * p.center + 1;
   const int gs = p.order[O.begin + s];
-  const int sup = p.support[O.begin + s];
-  A rp = 0, rm = 0, ip = 0, im = 0;
-  if (k <= sup) {
-    const A* hr = H + static_cast<int64_t>(gs * C) * hcols + p.center;
-    rp = __ldg(hr + k);
-    rm = __ldg(hr - k);
-    if (C == 2) {
-      ip = __ldg(hr + hcols + k);
-      im = __ldg(hr + hcols - k);
-    }
+  A ip = 0, im = 0;
+  // every tap of the octave's window is used (fdwt/cwt.py:566-578 slices the columns
+  // center-half .. center+half for all scales of the stage), so filters that are nonzero past a
+  // scale's support give the reference's results too
+  const A* hr = H + static_cast<int64_t>(gs * C) * hcols + p.center;
+  const A rp = __ldg(hr + k);
+  const A rm = __ldg(hr - k);
+  if (C == 2) {
+    ip = __ldg(hr + hcols + k);
+    im = __ldg(hr + hcols - k);
   }
   if (k == 0) {
     t[0] = rp;

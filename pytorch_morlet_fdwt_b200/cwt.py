@@ -26,6 +26,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 from torch import nn
+from torch.autograd.function import once_differentiable
 
 from . import _lib
 
@@ -223,6 +224,37 @@ def _cwt_forward(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor) -> torch.Te
     return y
 
 
+def _placeholder(like: torch.Tensor) -> torch.Tensor:
+    return like.new_zeros(0)
+
+
+def _cwt_backward(g: torch.Tensor, x: torch.Tensor, plan: MorletPlan, H: torch.Tensor,
+                  need_x: bool, need_h: bool):
+    """``(dL/dx (R, N), dL/dH (S*C, 2*center+1))`` from ``dL/dW (R, S, N, C)``: the adjoint
+    chain and the filter gradient in one kernel (plus the row reduction of dL/dH)."""
+    dev = _lib.require_cuda(g, x, H)
+    lib = _lib.load()
+    g = g.contiguous()
+    R, _, N, _ = g.shape
+    dt = g.dtype
+    Hd = _filters_on(H, g)
+    gx = torch.empty((R, N), device=dev, dtype=dt) if need_x else None
+    gh = torch.empty_like(Hd) if need_h else None
+    xd = x.detach().to(dt).contiguous() if need_h else None
+    code = _lib.dtype_code(dt)
+    with torch.cuda.device(dev):
+        nws = lib.fdwt_cwt_backward_workspace(code, R, N, ctypes.addressof(plan.capi()),
+                                              int(need_h))
+        ws = _lib.workspace(nws, dev)
+        st = lib.fdwt_cwt_backward(
+            code, R, N, None if xd is None else xd.data_ptr(), Hd.data_ptr(),
+            ctypes.addressof(plan.capi()), g.data_ptr(), None if gx is None else gx.data_ptr(),
+            None if gh is None else gh.data_ptr(), None if ws is None else ws.data_ptr(), nws,
+            _lib.stream_of(dev))
+    _lib.check(st, "fdwt_cwt_backward")
+    return gx, gh
+
+
 class _MorletCWTFunction(torch.autograd.Function):
     """All octaves of the transform in one autograd node (``fdwt/cwt.py:213-281``)."""
 
@@ -234,7 +266,52 @@ class _MorletCWTFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
-        raise NotImplementedError("CWT backward kernels are not built yet")
+        x, H = ctx.saved_tensors
+        need_x, need_h = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
+        if not (need_x or need_h):
+            return None, None, None
+        gx, gH = _CWTBackwardFunction.apply(g, x, ctx.plan, H, need_x, need_h)
+        return (gx if need_x else None), None, (gH.to(H.dtype) if need_h else None)
+
+
+class _CWTBackwardFunction(torch.autograd.Function):
+    """``(gx, gH) = (M_H^T g, dL/dH)`` of the transform.
+
+    ``gx`` is linear in ``g`` and ``gH`` bilinear in ``(x, g)``, so the derivatives of this node
+    are again the transform and these two outputs with other operands:
+    ``d/dg = M_H ggx + M_ggH x``, ``d/dx = M_ggH^T g``, ``d/dH = dL/dH(x = ggx, g)``.  The
+    transform therefore has derivatives of every order.
+    """
+
+    @staticmethod
+    def forward(ctx, g, x, plan: MorletPlan, H, need_x: bool, need_h: bool):
+        gx, gh = _cwt_backward(g, x, plan, H, need_x, need_h)
+        ctx.plan, ctx.flags = plan, (need_x, need_h)
+        ctx.save_for_backward(g, x, H)
+        gx = _placeholder(g) if gx is None else gx
+        gh = _placeholder(g) if gh is None else gh
+        return gx, gh
+
+    @staticmethod
+    def backward(ctx, ggx, ggH):
+        g, x, H = ctx.saved_tensors
+        plan = ctx.plan
+        need_x, need_h = ctx.flags
+        ggx = ggx if (need_x and ggx is not None) else None
+        ggH = ggH if (need_h and ggH is not None) else None
+        gg = gx2 = gH2 = None
+        if ctx.needs_input_grad[0]:
+            if ggx is not None:
+                gg = _MorletCWTFunction.apply(ggx, plan, H)
+            if ggH is not None:
+                t = _MorletCWTFunction.apply(x.to(g.dtype), plan, ggH)
+                gg = t if gg is None else gg + t
+        if ctx.needs_input_grad[1] and ggH is not None:
+            gx2, _ = _CWTBackwardFunction.apply(g, x, plan, ggH, True, False)
+        if ctx.needs_input_grad[3] and ggx is not None:
+            _, gH2 = _CWTBackwardFunction.apply(g, ggx, plan, H, False, True)
+            gH2 = gH2.to(H.dtype)
+        return gg, gx2, None, gH2, None, None
 
 
 def _fft_transform(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor) -> torch.Tensor:
@@ -385,6 +462,34 @@ def _mix_forward(x2, plan, H, a, b):
     return y
 
 
+def _mix_backward(gy, x, plan, H, a, b, need_x, need_h):
+    dev = _lib.require_cuda(gy, x, H, a, b)
+    lib = _lib.load()
+    R, N = x.shape
+    dt = x.dtype
+    gy = gy.to(dt).contiguous()
+    Hd = _filters_on(H, x)
+    a_ = a.detach().to(dt).contiguous()
+    b_ = b.detach().to(dt).contiguous()
+    D = a_.shape[0]
+    gx = torch.empty((R, N), device=dev, dtype=dt) if need_x else None
+    gh = torch.empty_like(Hd) if need_h else None
+    ga = torch.empty_like(a_)
+    gb = torch.empty_like(b_)
+    code = _lib.dtype_code(dt)
+    plan_p = ctypes.addressof(plan.capi())
+    with torch.cuda.device(dev):
+        nws = lib.fdwt_mix_backward_workspace(code, R, N, plan_p, D, int(need_h))
+        ws = _lib.workspace(nws, dev)
+        st = lib.fdwt_mix_backward(
+            code, R, N, x.data_ptr(), Hd.data_ptr(), plan_p, a_.data_ptr(), b_.data_ptr(), D,
+            gy.data_ptr(), None if gx is None else gx.data_ptr(),
+            None if gh is None else gh.data_ptr(), ga.data_ptr(), gb.data_ptr(),
+            None if ws is None else ws.data_ptr(), nws, _lib.stream_of(dev))
+    _lib.check(st, "fdwt_mix_backward")
+    return gx, gh, ga, gb
+
+
 class _MorletMixFunction(torch.autograd.Function):
     """``y[r, n] = sum_s a[d, s] |W_s[r, n]| + b[d, s] Re W_s[r, n]`` without materialising W
     (``fdwt/cwt.py:284-376``).  ``MIX_CHUNK_BYTES`` is kept for drop-in compatibility; the
@@ -399,8 +504,13 @@ class _MorletMixFunction(torch.autograd.Function):
         return _mix_forward(x, plan, H, a, b)
 
     @staticmethod
+    @once_differentiable
     def backward(ctx, gy):
-        raise NotImplementedError("mix backward kernels are not built yet")
+        x, H, a, b = ctx.saved_tensors
+        need_h = ctx.needs_input_grad[2]
+        gx, gH, ga, gb = _mix_backward(gy, x, ctx.plan, H, a, b, ctx.needs_input_grad[0],
+                                       need_h)
+        return (gx, None, gH.to(H.dtype) if need_h else None, ga.to(a.dtype), gb.to(b.dtype))
 
 
 def morlet_mix(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor, a: torch.Tensor,
@@ -432,6 +542,33 @@ def _softmax_forward(x2, plan, H, V, nch, tau):
     return out, m, l
 
 
+def _softmax_backward(gout, x, plan, H, V, nch, tau, m, l, out, need_x, need_h):
+    dev = _lib.require_cuda(gout, x, H, V)
+    lib = _lib.load()
+    R, N = x.shape
+    dt = x.dtype
+    gout = gout.to(dt).contiguous()
+    Hd = _filters_on(H, x)
+    V_ = V.detach().to(dt).contiguous()
+    v_pos = int(V_.dim() == 3)
+    gx = torch.empty((R, N), device=dev, dtype=dt) if need_x else None
+    gh = torch.empty_like(Hd) if need_h else None
+    gv = torch.empty_like(V_)
+    code = _lib.dtype_code(dt)
+    plan_p = ctypes.addressof(plan.capi())
+    with torch.cuda.device(dev):
+        nws = lib.fdwt_specsoftmax_backward_workspace(code, R, N, plan_p, v_pos, nch,
+                                                      int(need_h))
+        ws = _lib.workspace(nws, dev)
+        st = lib.fdwt_specsoftmax_backward(
+            code, R, N, x.data_ptr(), Hd.data_ptr(), plan_p, V_.data_ptr(), v_pos, nch,
+            1.0 / tau, m.data_ptr(), l.data_ptr(), out.data_ptr(), gout.data_ptr(),
+            None if gx is None else gx.data_ptr(), None if gh is None else gh.data_ptr(),
+            gv.data_ptr(), None if ws is None else ws.data_ptr(), nws, _lib.stream_of(dev))
+    _lib.check(st, "fdwt_specsoftmax_backward")
+    return gx, gh, gv
+
+
 class _SpectralSoftmaxFunction(torch.autograd.Function):
     """``out[r, n] = sum_f softmax_f(|W_f x_r|(n) / tau) * V_f[r, n]`` without materialising W
     (``fdwt/cwt.py:397-509``).  ``CHUNK_BYTES`` is kept for drop-in compatibility."""
@@ -448,8 +585,13 @@ class _SpectralSoftmaxFunction(torch.autograd.Function):
         return out
 
     @staticmethod
+    @once_differentiable
     def backward(ctx, gy):
-        raise NotImplementedError("spectral softmax backward kernels are not built yet")
+        x, H, V, m, l, out = ctx.saved_tensors
+        need_h = ctx.needs_input_grad[2]
+        gx, gH, gV = _softmax_backward(gy, x, ctx.plan, H, V, ctx.nch, ctx.tau, m, l, out,
+                                       ctx.needs_input_grad[0], need_h)
+        return (gx, None, gH.to(H.dtype) if need_h else None, gV.to(V.dtype), None, None, None)
 
 
 def spectral_softmax(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor, V: torch.Tensor,
