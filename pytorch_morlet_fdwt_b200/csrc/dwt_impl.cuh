@@ -762,6 +762,14 @@ dwt_synthesis_kernel(const __grid_constant__ Params<typename AccOf<T>::type, LM>
 
 constexpr int kLM[] = {2, 4, 6, 8, 10, 12, 16, 20, 24, 32, 40, 64};
 
+}  // namespace dwtk
+}  // namespace fdwt
+
+#include "dwt_syn_tile.cuh"
+
+namespace fdwt {
+namespace dwtk {
+
 inline int pick_lm(int L) {
   for (int lm : kLM)
     if (L <= lm) return lm;
@@ -952,6 +960,15 @@ int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
   using A = typename AccOf<T>::type;
   using C = Cfg<T, LM>;
   const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
+  if (!ANALYSIS) {
+    // independent output tiles when their staging fits; the cluster kernel otherwise
+    const int ts = run_syn_tiles<T, LM>(rows, src0, lv, dst_final, h0, h1, L, off, stream,
+                                        ws_needed != nullptr);
+    if (ts != FDWT_ERR_UNSUPPORTED) {
+      if (ws_needed) *ws_needed = 0;
+      return ts;
+    }
+  }
   if (!ANALYSIS) {
     for (auto& l : lv) {
       l.fold_n = fold_count(l.n_in, l.n_coef, off, LM, l.mode);
