@@ -71,8 +71,18 @@ struct TileGeo {              // coefficient segments of one level (a and d shar
   int32_t origin[kTileSegs];  // coefficient stored at padded index 0
 };
 
-struct TileOut {  // outputs of one level that the tile computes
-  int32_t s[kTileSegs], e[kTileSegs];
+// Everything one level of a tile needs, precomputed by the plan (one shared-memory record per
+// level, so that a level starts with independent loads rather than a chain of dependent ones).
+struct LevelInfo {
+  int32_t n_out, nc, mode, P;
+  int32_t nleft, nright, edge, d_base;   // edge: the tile has outputs onto which exterior
+                                          // positions fold
+  int32_t ext_slot[2], ext_org[2], ext_len[2];  // segments read by the left / right exterior
+  int32_t js[kTileSegs], je[kTileSegs];          // output ranges
+  int32_t src_slot[kTileSegs], src_org[kTileSegs];  // coefficient segment feeding each range
+  int32_t dst_slot[kTileSegs], dst_org[kTileSegs];  // where level i-1 keeps each range
+  int32_t zl_end[kTileSegs];                    // margin cells to zero: [0, zl_end) and
+  int32_t zr_beg[kTileSegs], zr_end[kTileSegs]; // [zr_beg, zr_end) of each output segment
 };
 
 // ------------------------------------------------------------------------------ planning
@@ -93,25 +103,41 @@ __host__ __device__ __forceinline__ void cone(int ms, int me, int off, int LM, i
 // parameter loads), keeps its own level's main range and writes its level's geometry; the
 // finest level near a row end comes from a ballot.
 template <typename A, int LM>
-__device__ void plan_tile(const TileParams<A, LM>& p, int t, TileGeo* geo, TileOut* outs) {
+__device__ void plan_tile(const TileParams<A, LM>& p, int t, TileGeo* geo, LevelInfo* info) {
   const int J = p.J;
   const int lane = threadIdx.x & 31;
-  int my_nc = 0, my_full = 0;
+  int my_nc = 0, my_full = 0, my_nout = 0, my_mode = 0, my_P = 0, my_dbase = 0;
+  int my_slot[kTileSegs] = {0, 0, 0};
+  int f_nc = 0, f_slot[kTileSegs] = {0, 0, 0}, f_cap[kTileSegs] = {0, 0, 0};  // level lane-1
   int ms = t * p.T;
   int me = min(p.lv[0].n_out, ms + p.T);
   int my_ms = 0, my_me = 0;
   bool my_edge = false;
   for (int i = 0; i < J; ++i) {
     // same address in every lane: broadcast constant loads
-    const int n_out = p.lv[i].n_out;
-    const int nc = p.lv[i].nc;
-    const int full = p.lv[i].full;
+    const TileLevel& L = p.lv[i];
+    const int n_out = L.n_out;
+    const int nc = L.nc;
     if (lane == i) {
       my_nc = nc;
-      my_full = full;
+      my_full = L.full;
+      my_nout = n_out;
+      my_mode = L.mode;
+      my_P = L.P;
+      my_dbase = L.d_base;
+#pragma unroll
+      for (int s = 0; s < kTileSegs; ++s) my_slot[s] = L.slot[s];
       my_ms = ms;
       my_me = me;
       my_edge = ms < LM || me > n_out - LM;
+    }
+    if (lane == i + 1) {
+      f_nc = nc;
+#pragma unroll
+      for (int s = 0; s < kTileSegs; ++s) {
+        f_slot[s] = L.slot[s];
+        f_cap[s] = L.cap[s];
+      }
     }
     int lo, hi;
     cone(ms, me, p.off, LM, nc, lo, hi);
@@ -120,7 +146,7 @@ __device__ void plan_tile(const TileParams<A, LM>& p, int t, TileGeo* geo, TileO
   }
   const unsigned edges = __ballot_sync(0xffffffffu, lane < J && my_edge);
   const int first_edge = edges ? __ffs(edges) - 1 : J;
-  int st[kTileSegs] = {0, 0, 0}, ln[kTileSegs] = {0, 0, 0};
+  int st[kTileSegs] = {0, 0, 0}, ln[kTileSegs] = {0, 0, 0}, org[kTileSegs];
   if (lane < J) {
     if (my_full) {
       ln[0] = my_nc;
@@ -134,33 +160,77 @@ __device__ void plan_tile(const TileParams<A, LM>& p, int t, TileGeo* geo, TileO
       st[2] = max(0, my_nc - p.W);
       ln[2] = win ? my_nc - st[2] : 0;
     }
+  }
+#pragma unroll
+  for (int s = 0; s < kTileSegs; ++s) {
+    // origin: at least ML below the segment start, with the launch-wide residue mod 4
+    const int lo = st[s] - p.ML;
+    org[s] = lo - ((lo - p.origin_res) & 3);
+  }
+  if (lane < J) {
     TileGeo& G = geo[lane];
 #pragma unroll
     for (int s = 0; s < kTileSegs; ++s) {
       G.start[s] = st[s];
       G.len[s] = ln[s];
-      // origin: at least ML below the segment start, with the launch-wide residue mod 4
-      const int lo = st[s] - p.ML;
-      G.origin[s] = lo - ((lo - p.origin_res) & 3);
+      G.origin[s] = org[s];
     }
   }
-  // outputs of level i: the coefficient segments of level i-1, or the main range of y
+  // the output segments of level i are the coefficient segments of level i-1
+  int ps[kTileSegs], pl[kTileSegs], porg[kTileSegs];
 #pragma unroll
   for (int s = 0; s < kTileSegs; ++s) {
-    const int ps = __shfl_up_sync(0xffffffffu, st[s], 1);
-    const int pl = __shfl_up_sync(0xffffffffu, ln[s], 1);
-    if (lane < J && lane > 0) {
-      outs[lane].s[s] = ps;
-      outs[lane].e[s] = ps + pl;
-    }
+    ps[s] = __shfl_up_sync(0xffffffffu, st[s], 1);
+    pl[s] = __shfl_up_sync(0xffffffffu, ln[s], 1);
+    porg[s] = __shfl_up_sync(0xffffffffu, org[s], 1);
   }
-  if (lane == 0) {  // y: the main range only, fed by the main (or full) coefficient segment
-    TileOut& O = outs[0];
-    O.s[0] = my_full ? my_ms : 0;
-    O.e[0] = my_full ? my_me : 0;
-    O.s[1] = my_full ? 0 : my_ms;
-    O.e[1] = my_full ? 0 : my_me;
-    O.s[2] = O.e[2] = 0;
+  if (lane < J) {
+    LevelInfo& I = info[lane];
+    I.n_out = my_nout;
+    I.nc = my_nc;
+    I.mode = my_mode;
+    I.P = my_P;
+    I.d_base = my_dbase;
+    const int pmin = p.off - (LM - 1);
+    const int pmax = 2 * (my_nc - 1) + p.off;
+    I.nleft = max(0, min(-1, pmax) - pmin + 1);
+    I.nright = max(0, pmax - max(my_nout, pmin) + 1);
+    const bool folds = my_mode != FDWT_MODE_ZERO && I.nleft + I.nright > 0;
+    const int rs = my_full ? 0 : 2;
+    I.ext_slot[0] = my_slot[0];
+    I.ext_org[0] = org[0];
+    I.ext_len[0] = ln[0];
+    I.ext_slot[1] = my_slot[rs];
+    I.ext_org[1] = org[rs];
+    I.ext_len[1] = ln[rs];
+    bool edge = false;
+#pragma unroll
+    for (int s = 0; s < kTileSegs; ++s) {
+      int js, je;
+      if (lane == 0) {  // y: the main range only, fed by the main (or full) segment
+        const bool mine = my_full ? s == 0 : s == 1;
+        js = mine ? my_ms : 0;
+        je = mine ? my_me : 0;
+      } else {
+        js = ps[s];
+        je = ps[s] + pl[s];
+      }
+      I.js[s] = js;
+      I.je[s] = je;
+      edge |= je > js && (js < LM || je > my_nout - LM);
+      const int ss = my_full ? 0 : s;
+      I.src_slot[s] = my_slot[ss];
+      I.src_org[s] = org[ss];
+      I.dst_slot[s] = f_slot[s];
+      I.dst_org[s] = porg[s];
+      // margins of the output segment that stand for coefficients outside [0, nc)
+      const int s0 = ps[s] - porg[s];
+      const bool live = lane > 0 && pl[s] > 0;
+      I.zl_end[s] = (live && ps[s] == 0) ? s0 : 0;
+      I.zr_beg[s] = s0 + pl[s];
+      I.zr_end[s] = (live && ps[s] + pl[s] == f_nc) ? f_cap[s] : 0;
+    }
+    I.edge = edge && folds;
   }
 }
 
@@ -330,14 +400,14 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
   A* dreg = reinterpret_cast<A*>(smem);
   A* abufs[2] = {dreg + p.d_len, dreg + p.d_len + p.abuf_len[0]};  // a_i lives in abufs[i & 1]
   __shared__ TileGeo geo[kMaxLevels];
-  __shared__ TileOut outs[kMaxLevels];
+  __shared__ LevelInfo info[kMaxLevels];
   __shared__ A zl[2 * LM + 8], zr[2 * LM + 8];
   __shared__ A zadd[2 * LM];  // folded exterior values per edge-zone output (see zone_index)
 
   const int64_t row = blockIdx.x / p.tiles;
   const int t = static_cast<int>(blockIdx.x % p.tiles);
   const int J = p.J;
-  if (threadIdx.x < 32) plan_tile<A, LM>(p, t, geo, outs);
+  if (threadIdx.x < 32) plan_tile<A, LM>(p, t, geo, info);
   __syncthreads();
 
   // stage every level's details and the coarsest approximation: one warp per segment
@@ -374,57 +444,37 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
     for (int k = 0; k < 2 * TQ; ++k) soff[k] = k + ((r + k) >> TPS);
   }
   T* yrow = static_cast<T*>(p.y) + row * p.lv[0].n_out;
+  const int pmin = p.off - (LM - 1);
   for (int i = J - 1; i >= 0; --i) {
-    const TileLevel& L = p.lv[i];
-    const TileGeo& G = geo[i];
+    const LevelInfo& I = info[i];
     const A* acur = abufs[i & 1];
     A* anext = abufs[(i + 1) & 1];
-    const A* dcur = dreg + L.d_base;
-    const int n_out = L.n_out;
-    const int pmin = p.off - (LM - 1);
-    const int pmax = 2 * (L.nc - 1) + p.off;
-    const int nleft = max(0, min(-1, pmax) - pmin + 1);
-    const int nright = max(0, pmax - max(n_out, pmin) + 1);
-    const int rs = L.full ? 0 : 2;  // segment holding the coefficients near the right end
-    const bool folds = L.mode != FDWT_MODE_ZERO && (nleft > 0 || nright > 0);
-    const TileOut& O = outs[i];
-    // does this tile compute outputs in the edge zones [0, LM) or [n_out - LM, n_out)?
-    bool edge = false;
-    for (int s = 0; s < kTileSegs; ++s)
-      edge |= O.e[s] > O.s[s] && (O.s[s] < LM || O.e[s] > n_out - LM);
-    edge = edge && folds;
+    const A* dcur = dreg + I.d_base;
+    const int n_out = I.n_out, nc = I.nc;
+    const int nleft = I.nleft, nright = I.nright;
+    const bool edge = I.edge != 0;
     if (edge) {
       // exterior positions that fold back into the row
       for (int k = threadIdx.x; k < nleft + nright; k += TNT) {
-        if (k < nleft) {
-          zl[k] = G.len[0] > 0 ? z_at<A, LM>(p, pmin + k, acur + L.slot[0], dcur + L.slot[0],
-                                             G.origin[0], L.nc)
-                               : A(0);
-        } else {
-          const int kk = k - nleft;
-          zr[kk] = G.len[rs] > 0 ? z_at<A, LM>(p, max(n_out, pmin) + kk, acur + L.slot[rs],
-                                               dcur + L.slot[rs], G.origin[rs], L.nc)
-                                 : A(0);
-        }
+        const int side = k < nleft ? 0 : 1;
+        const int pos = side == 0 ? pmin + k : max(n_out, pmin) + (k - nleft);
+        const A z = I.ext_len[side] > 0
+                        ? z_at<A, LM>(p, pos, acur + I.ext_slot[side], dcur + I.ext_slot[side],
+                                      I.ext_org[side], nc)
+                        : A(0);
+        if (side == 0) zl[k] = z;
+        else zr[k - nleft] = z;
       }
       for (int k = threadIdx.x; k < 2 * LM; k += TNT) zadd[k] = A(0);
     }
     // in the next level's buffer, margins that stand for coefficients outside [0, nc) must read
     // as zero (other margin cells only feed outputs that are discarded); they are disjoint from
     // the cells this level's jobs write
-    if (i > 0) {
-      const TileLevel& F = p.lv[i - 1];
-      const TileGeo& FG = geo[i - 1];
-      for (int s = 0; s < kTileSegs; ++s) {
-        if (FG.len[s] == 0) continue;
-        A* b = anext + F.slot[s];
-        const int s0 = FG.start[s] - FG.origin[s];
-        if (FG.start[s] == 0)
-          for (int k = threadIdx.x; k < s0; k += TNT) b[sidx<TPS>(k)] = A(0);
-        if (FG.start[s] + FG.len[s] == F.nc)
-          for (int k = s0 + FG.len[s] + threadIdx.x; k < F.cap[s]; k += TNT)
-            b[sidx<TPS>(k)] = A(0);
-      }
+#pragma unroll
+    for (int s = 0; s < kTileSegs; ++s) {
+      A* b = anext + I.dst_slot[s];
+      for (int k = threadIdx.x; k < I.zl_end[s]; k += TNT) b[sidx<TPS>(k)] = A(0);
+      for (int k = I.zr_beg[s] + threadIdx.x; k < I.zr_end[s]; k += TNT) b[sidx<TPS>(k)] = A(0);
     }
     if (edge) {
       __syncthreads();
@@ -432,7 +482,7 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
       if (threadIdx.x == 0) {
         for (int e = 0; e < nleft + nright; ++e) {
           const int pe = e < nleft ? pmin + e : max(n_out, pmin) + (e - nleft);
-          const int q = ext32(pe, n_out, L.mode, L.P);
+          const int q = ext32(pe, n_out, I.mode, I.P);
           const int zi = zone_index(q, n_out, LM);
           if (zi >= 0) zadd[zi] += e < nleft ? zl[e] : zr[e - nleft];
         }
@@ -440,21 +490,16 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
       __syncthreads();
     }
 
+#pragma unroll 1
     for (int s = 0; s < kTileSegs; ++s) {
-      const int js = O.s[s], je = O.e[s];
+      const int js = I.js[s], je = I.je[s];
       if (je <= js) continue;
-      const int ss = L.full ? 0 : s;  // coefficient segment feeding this output segment
-      const A* ab = acur + L.slot[ss];
-      const A* db = dcur + L.slot[ss];
-      const int origin = G.origin[ss];
+      const A* ab = acur + I.src_slot[s];
+      const A* db = dcur + I.src_slot[s];
+      const int origin = I.src_org[s];
       const int i0 = js >> 3, i1 = (je + 7) >> 3;
-      // the output destination of level i
-      A* dst = nullptr;
-      int dorigin = 0;
-      if (i > 0) {
-        dst = anext + p.lv[i - 1].slot[s];
-        dorigin = geo[i - 1].origin[s];
-      }
+      A* dst = anext + I.dst_slot[s];  // level i > 0: the next level's coefficients
+      const int dorigin = I.dst_org[s];
       for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += TNT) {
         const int p0 = it * 8;
         const int o0 = (p0 - p.off - C0) >> 1;  // exact: p0 - off - C0 is even
@@ -593,7 +638,7 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
   }
   const size_t smem = static_cast<size_t>(d_len + abuf[0] + abuf[1]) * sizeof(A) + 16;
   const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048 -
-                        sizeof(TileGeo) * kMaxLevels - sizeof(TileOut) * kMaxLevels -
+                        sizeof(TileGeo) * kMaxLevels - sizeof(LevelInfo) * kMaxLevels -
                         2 * (2 * LM + 8) * sizeof(A) - 2 * LM * sizeof(A);
   if (smem > budget) return FDWT_ERR_UNSUPPORTED;
   if (rows * p.tiles > 0x7fffffffLL) return FDWT_ERR_UNSUPPORTED;
