@@ -28,6 +28,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 import numpy as np
@@ -37,6 +38,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "DWT/CWT achieved HBM GB/s (% of B200 peak); Morlet mixer tokens/s fwd+bwd"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) per full-size launch, from one ncu capture of each kernel on 512 of
+# the 2048 rows scaled by 4 (traffic grows with the rows); the captures are summarised in
+# profiles/dwt_cfg2_kernels.txt (a text file, not this build's notes)
+TRAFFIC_PER_LAUNCH = {
+    "dwt_analysis_kernel<float,16>": 897_000_000,
+    "dwt_syn_tile_kernel<float,16,0>": 914_000_000,
+}
 
 
 # ------------------------------------------------------------------------------ helpers
@@ -51,57 +59,66 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clock and clock-event reasons of this rank's GPU, sampled through NVML (read only)
+    every few milliseconds by a background thread while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    def __init__(self, device_index: int, period_s: float = 0.004):
+        self.index = device_index
+        self.period = period_s
+        self.samples, self.reasons, self.smax = [], set(), None
+        self.handle = None
+        self.thread = None
+        self.stop = threading.Event()
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.out = os.path.join("/tmp", f"fdwt_clocks_{os.getpid()}.csv")
+    def _open(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.index)
+        uuid = getattr(props, "uuid", None)
+        if uuid is not None:
+            try:
+                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}")
+            except pynvml.NVMLError:
+                pass
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+
+    def _run(self, nv):
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap,
+                "hw_power_brake": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown}
+        while not self.stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.reasons.update(k for k, b in bits.items() if r & b)
+            except nv.NVMLError:
+                break
+            time.sleep(self.period)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=open(self.out, "w"), stderr=subprocess.DEVNULL)
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            nv, self.handle = self._open()
+            self.smax = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, args=(nv,), daemon=True)
+            self.thread.start()
+        except Exception:  # no NVML: reported as unsampled
+            self.thread = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
 
     def summary(self):
-        if self.proc is None or not os.path.exists(self.out):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.out):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for name, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        os.unlink(self.out)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "samples": len(sm),
-                "reasons": sorted(reasons)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.smax, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.smax,
+                "samples": len(self.samples), "reasons": sorted(self.reasons)}
 
 
 # ------------------------------------------------------------------------------ workload
@@ -180,6 +197,8 @@ def run_ours(args, rank, world, local_rank, pool):
     dev = torch.device("cuda", local_rank)
     torch.manual_seed(1234 + rank)
     shape = CFG2["shape"]
+    if args.rows is not None:
+        shape = (1, args.rows, shape[-1])
     bank = F.get_filter_bank(CFG2["wavelet"])
     mode, level = CFG2["mode"], CFG2["level"]
     x0 = torch.randn(shape, device=dev)
@@ -203,8 +222,11 @@ def run_ours(args, rank, world, local_rank, pool):
         step(x)
     torch.cuda.synchronize()
 
-    # dominant kernel: the fused multilevel analysis launch of wavedec, timed per launch
-    ka, kb = ([torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] for _ in range(2))
+    # per-launch device time of the two kernels of the step: the fused multilevel analysis
+    # (wavedec; also the waverec backward) and the tile synthesis (waverec; also the wavedec
+    # backward), each timed on its forward call
+    ka, kb, kc = ([torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+                  for _ in range(3))
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _lib.launch_count()
     barrier()
@@ -217,19 +239,26 @@ def run_ours(args, rank, world, local_rank, pool):
             coeffs = F.wavedec(x, bank, mode, level)
             kb[i].record()
             y = F.waverec(coeffs, bank, mode)
+            kc[i].record()
             torch.autograd.backward(y, gy)
         end.record()
         torch.cuda.synchronize()
     barrier()
     launches = _lib.launch_count() - launches0
     ms = start.elapsed_time(end)
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ka, kb))
-    t = torch.tensor([ms, kern_ms], device=dev, dtype=torch.float64)
+    ana_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ka, kb))
+    syn_ms = statistics.mean(b.elapsed_time(c) for b, c in zip(kb, kc))
+    t = torch.tensor([ms, ana_ms, syn_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, kern_ms = float(t[0]), float(t[1])
+    ms, ana_ms, syn_ms = float(t[0]), float(t[1]), float(t[2])
 
     # end to end through the public API with host buffers (pinned), every step
+    e2e_steps = max(1, min(args.steps, 10))
+    e2e_ms = float("nan")
+    if args.no_e2e:
+        return _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms,
+                            launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
     xh = x0.cpu().pin_memory()
     gh = torch.empty_like(xh).pin_memory()
     xd = torch.empty_like(x0)
@@ -240,7 +269,6 @@ def run_ours(args, rank, world, local_rank, pool):
         gh.copy_(xe.grad, non_blocking=True)
         xe.grad = None
     torch.cuda.synchronize()
-    e2e_steps = max(1, min(args.steps, 10))
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -257,11 +285,22 @@ def run_ours(args, rank, world, local_rank, pool):
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te[0])
+    return _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms,
+                        launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
 
+
+def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms, launches,
+                 clk, pool, x0, e2e_steps, e2e_ms, shape):
     if rank != 0:
         return None
     peak, peak_src = peaks()
     value = step_bytes * args.steps * world / (ms / 1e3) / 1e9
+    kernels = {
+        "dwt_analysis_kernel<float,16>": ana_ms,
+        "dwt_syn_tile_kernel<float,16,0>": syn_ms,
+    }
+    dominant = max(kernels, key=kernels.get)
+    kern_ms = kernels[dominant]
     achieved = dir_bytes_row * R / (kern_ms / 1e3) / 1e9
     line = {
         "metric": METRIC,
@@ -278,20 +317,22 @@ def run_ours(args, rank, world, local_rank, pool):
         "data": "synthetic i.i.d. N(0,1), seeded per rank",
         "config": {
             "workload": "cfg2: db8 periodization level-8 wavedec + waverec + backward through "
-                        "both, x float32 (16,128,65536) per GPU",
+                        f"both, x float32 {tuple(shape)} per GPU",
             "algorithmic_bytes_per_step": step_bytes,
             "l2": "inputs larger than L2 (512 MiB per array)",
             "parallelism": f"rows sharded by rank, {world} GPU(s), no collective",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "dwt_analysis_kernel<float,16> (fused 8-level wavedec)",
+            "bound": "hbm", "kernel": dominant,
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_src,
             "algorithmic_bytes_per_launch": dir_bytes_row * R,
-            "launch_ms": round(kern_ms, 4), "traffic": None,
+            "launch_ms": round(kern_ms, 4),
+            "traffic": TRAFFIC_PER_LAUNCH.get(dominant),
+            "kernels_ms_per_launch": {k: round(v, 4) for k, v in kernels.items()},
         },
         "gpu_launches": int(launches),
-        "e2e": {
+        "e2e": None if args.no_e2e else {
             "value": round(step_bytes * e2e_steps * world / (e2e_ms / 1e3) / 1e9, 2),
             "unit": "GB/s",
             "h2d_bytes_per_step": x0.numel() * 4,
@@ -339,19 +380,349 @@ def run_reference(args, pool):
     }
 
 
+# ------------------------------------------------------------------------------ other configs
+#
+# The other baseline configs (2, 3, 4), measured the same way on demand with
+# --config; each prints its own line.  The forward and the backward calls are timed separately
+# with CUDA events; the kernel named in "roofline" is the one with the larger share.
+
+
+def _cfg_cwt_plan(learnable):
+    import pytorch_morlet_fdwt_b200 as F
+    return F.CWT1D(freqs=np.logspace(-0.3, 2, 40), fs=250.0, norm="l1", learnable=learnable,
+                   learnable_w0=learnable)
+
+
+def _wl_cfg1():
+    import torch
+    import pytorch_morlet_fdwt_b200 as F
+    from oracle.dwt_oracle import dwt_coeff_len
+    n, lv = 2500, 5
+    lens, cur = [], n
+    for _ in range(lv):
+        cur = dwt_coeff_len(cur, 8, "symmetric")
+        lens.append(cur)
+    rows = 32 * 64
+    per_dir = rows * (n + sum(lens) + lens[-1]) * 4
+
+    def setup(dev):
+        return {"x": torch.randn(32, 64, n, device=dev).requires_grad_(),
+                "bank": F.get_filter_bank("db4")}
+
+    def fwd(st):
+        st["c"] = F.wavedec(st["x"], st["bank"], "symmetric", lv)
+        st["y"] = F.waverec([c.detach() for c in st["c"]], st["bank"], "symmetric")
+
+    def bwd(st):
+        st["x"].grad = None
+        sum((c * c).sum() for c in st["c"]).backward()
+
+    def cpu(rows_s):
+        from oracle import dwt_oracle as D
+        b = F.get_filter_bank("db4")
+        tb = (b.dec_lo, b.dec_hi, b.rec_lo, b.rec_hi)
+        x = np.random.default_rng(0).standard_normal((rows_s, n)).astype(np.float32)
+        t = time.perf_counter()
+        c = D.wavedec(x, tb, "symmetric", lv)
+        D.waverec(c, tb, "symmetric")
+        D.wavedec_vjp(n, [2 * v for v in c], tb, "symmetric")
+        return time.perf_counter() - t
+
+    return dict(name="cfg1: db4 symmetric level-5 wavedec, waverec and the backward of "
+                     "sum(coeffs^2), x float32 (32,64,2500)",
+                unit="GB/s", per_step=3 * per_dir, rows=rows, setup=setup, fwd=fwd, bwd=bwd,
+                cpu=cpu, cpu_rows=2048, dtype="f32",
+                kernels=("dwt_analysis_kernel + dwt_syn_tile_kernel (waverec)",
+                         "dwt_syn_tile_kernel (backward)"),
+                fwd_bytes=2 * per_dir, bwd_bytes=per_dir)
+
+
+def _wl_cfg3(learnable, rows=None):
+    import torch
+    from oracle import cwt_oracle as C
+    shape = (32 if rows is None else max(1, rows // 64), 64, 2500)
+    rows = shape[0] * shape[1]
+    x_bytes = rows * 2500 * 4
+    w_bytes = rows * 40 * 2500 * 8
+
+    def setup(dev):
+        m = _cfg_cwt_plan(learnable).to(dev)
+        return {"m": m, "x": torch.randn(shape, device=dev).requires_grad_(learnable)}
+
+    def fwd(st):
+        st["y"] = st["m"](st["x"])
+
+    def bwd(st):
+        if learnable:
+            st["x"].grad = None
+            st["m"].zero_grad()
+            torch.view_as_real(st["y"]).square().sum().backward()
+
+    def cpu(rows_s):
+        m = _cfg_cwt_plan(learnable)
+        po = C.Plan(m.plan.scales, norm="l1", support_margin=1.25 if learnable else 1.0)
+        ls = torch.tensor(m.plan.scales, dtype=torch.float64).log().requires_grad_(learnable)
+        w0 = torch.tensor(6.0, dtype=torch.float64, requires_grad=learnable)
+        x = torch.randn(rows_s, 2500, dtype=torch.float64, requires_grad=learnable)
+        t = time.perf_counter()
+        W = C.apply_plan(x, po, po.filters(ls.exp(), w0))
+        if learnable:
+            W.abs().square().sum().backward()
+        return time.perf_counter() - t
+
+    fb = x_bytes + w_bytes
+    bb = w_bytes + 2 * x_bytes if learnable else 0
+    name = ("cfg3: Morlet CWT fast, 40 freqs logspace(-0.3,2) @ 250 Hz, l1, x float32 "
+            f"{shape} -> complex64 ({shape[0]},64,40,2500)")
+    if learnable:
+        name += "; learnable scales and w0, backward of sum |W|^2"
+    return dict(name=name, unit="GB/s", per_step=fb + bb, rows=rows, setup=setup, fwd=fwd,
+                bwd=bwd, cpu=cpu, cpu_rows=32 if learnable else 64, dtype="f32",
+                kernels=("cwt_forward_kernel<float,float,0>", "cwt_backward_kernel<float,0>"),
+                fwd_bytes=fb, bwd_bytes=bb)
+
+
+def _wl_cfg4():
+    import torch
+    import pytorch_morlet_fdwt_b200 as F
+    from oracle import cwt_oracle as C
+    freqs = np.logspace(0, 1.8, 16).tolist()
+
+    def setup(dev):
+        torch.manual_seed(0)
+        m = F.MorletTokenMixer(256, freqs=freqs, fs=250).to(dev)
+        return {"m": m, "x": torch.randn(8, 4096, 256, device=dev).requires_grad_()}
+
+    def fwd(st):
+        st["y"] = st["m"](st["x"])
+
+    def bwd(st):
+        st["x"].grad = None
+        st["m"].zero_grad()
+        st["y"].square().sum().backward()
+
+    def cpu(batch):
+        torch.manual_seed(0)
+        m = F.MorletTokenMixer(256, freqs=freqs, fs=250).double()
+        po = C.Plan(m.cwt.plan.scales, support_margin=1.25)
+        x = torch.randn(batch, 4096, 256, dtype=torch.float64, requires_grad=True)
+        ls = m.cwt.log_scales.detach().double().requires_grad_()
+        t = time.perf_counter()
+        y = C.token_mixer(x, po, po.filters(ls.exp(), m.cwt.w0_value), m.mag_weight,
+                          m.phase_weight, m.bias, m.out_proj.weight, m.out_proj.bias)
+        y.square().sum().backward()
+        return time.perf_counter() - t
+
+    return dict(name="cfg4: MorletTokenMixer dim 256, 16 freqs logspace(0,1.8) @ 250 Hz, "
+                     "x float32 (8,4096,256), forward + backward",
+                unit="tokens/s", per_step=8 * 4096, rows=8 * 256, setup=setup, fwd=fwd, bwd=bwd,
+                cpu=cpu, cpu_rows=1, cpu_unit_per_row=4096, cpu_reps=1, dtype="f32",
+                kernels=("cwt_forward_kernel<float,float,1> (mix)",
+                         "cwt_backward_kernel<float,1> (mix)"),
+                fwd_bytes=2 * 8 * 4096 * 256 * 4, bwd_bytes=3 * 8 * 4096 * 256 * 4)
+
+
+def _wl_cfg5(channel_mix):
+    import torch
+    import pytorch_morlet_fdwt_b200 as F
+    from oracle import cwt_oracle as C
+    cls = F.MorletChannelMixAttention if channel_mix else F.MorletAttention
+
+    def setup(dev):
+        torch.manual_seed(0)
+        m = cls(num_channels=19, hidden_dim=200).to(dev)
+        return {"m": m, "x": torch.randn(64, 4, 19, 30, 200, device=dev).requires_grad_()}
+
+    def fwd(st):
+        st["y"] = st["m"](st["x"])
+
+    def bwd(st):
+        st["x"].grad = None
+        st["m"].zero_grad()
+        st["y"].square().sum().backward()
+
+    def cpu(batch):
+        torch.manual_seed(0)
+        m = cls(num_channels=19, hidden_dim=200).double()
+        po = C.Plan(m.cwt.plan.scales, support_margin=1.25)
+        x = torch.randn(batch, 4, 19, 30, 200, dtype=torch.float64, requires_grad=True)
+        ls = m.cwt.log_scales.detach().double().requires_grad_()
+        w0 = torch.tensor(m.cwt.w0_value, dtype=torch.float64, requires_grad=True)
+        H = po.filters(ls.exp(), w0)
+        t = time.perf_counter()
+        if channel_mix:
+            y = C.channel_mix_attention(x, po, H, m.freq_to_channel, m.temperature)
+        else:
+            y = C.attention(x, po, H, m.freq_weight, m.temperature)
+        y.square().sum().backward()
+        return time.perf_counter() - t
+
+    name = ("cfg5: Morlet" + ("ChannelMix" if channel_mix else "") + "Attention, 19 channels, "
+            "hidden 200, x float32 (64,4,19,30,200), forward + backward")
+    return dict(name=name, unit="tokens/s", per_step=64 * 19 * 30, rows=64 * 4 * 19,
+                setup=setup, fwd=fwd, bwd=bwd, cpu=cpu, cpu_rows=1, cpu_unit_per_row=19 * 30,
+                dtype="f32",
+                kernels=("cwt_forward_kernel<float,float,2> (spectral softmax)",
+                         "cwt_backward_kernel<float,2> (spectral softmax)"),
+                fwd_bytes=2 * 64 * 4 * 19 * 6000 * 4, bwd_bytes=3 * 64 * 4 * 19 * 6000 * 4)
+
+
+WORKLOADS = {
+    "cfg1": _wl_cfg1,
+    "cfg3": lambda rows=None: _wl_cfg3(False, rows),
+    "cfg3l": lambda rows=None: _wl_cfg3(True, rows),
+    "cfg4": _wl_cfg4,
+    "cfg5": lambda: _wl_cfg5(False),
+    "cfg5c": lambda: _wl_cfg5(True),
+}
+
+
+def run_config(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from pytorch_morlet_fdwt_b200 import _lib
+    W = WORKLOADS[args.config](args.rows) if args.rows else WORKLOADS[args.config]()
+    # CPU baseline first (before any CUDA work), rank 0 at N=1
+    cpu_line = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import torch as _t
+        _t.set_num_threads(os.cpu_count() or 1)
+        reps = W.get("cpu_reps", 3)
+        if reps > 1:
+            W["cpu"](W["cpu_rows"])  # warm-up
+        times = [W["cpu"](W["cpu_rows"]) for _ in range(reps)]
+        tc = statistics.median(times)
+        units = W.get("cpu_unit_per_row")
+        per = (W["cpu_rows"] * units) if units else W["per_step"] * W["cpu_rows"] / W["rows"]
+        cpu_line = {"value": round(per / tc / (1e9 if W["unit"] == "GB/s" else 1), 4),
+                    "unit": W["unit"], "cores": os.cpu_count(), "kind": "port",
+                    "sample": f"{W['cpu_rows']} {'batch entries' if units else 'rows'} of the "
+                              f"workload through the fp64 CPU oracle (torch, all cores), median "
+                              f"of {reps} ({tc:.2f} s each)"}
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(100 + rank)
+    st = W["setup"](dev)
+    for _ in range(args.warmup):
+        W["fwd"](st)
+        W["bwd"](st)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    l0 = _lib.launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for e in ev:
+            e[0].record()
+            W["fwd"](st)
+            e[1].record()
+            W["bwd"](st)
+            e[2].record()
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - l0
+    ms = ev[0][0].elapsed_time(ev[-1][2])
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    t = torch.tensor([ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.destroy_process_group()
+    ms, fwd_ms, bwd_ms = (float(v) for v in t)
+    if rank != 0:
+        return 0
+    scale = 1e9 if W["unit"] == "GB/s" else 1.0
+    value = W["per_step"] * args.steps * world / (ms / 1e3) / scale
+    peak, peak_src = peaks()
+    dom = 0 if fwd_ms >= bwd_ms or W["bwd_bytes"] == 0 else 1
+    k_ms = fwd_ms if dom == 0 else bwd_ms
+    k_bytes = W["fwd_bytes"] if dom == 0 else W["bwd_bytes"]
+    achieved = k_bytes / (k_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": W["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": W["dtype"],
+        "data": "synthetic i.i.d. N(0,1), random-init parameters, seeded",
+        "config": {"workload": W["name"], "l2": "outputs larger than L2" if W["unit"] == "GB/s"
+                   else "inputs and scalograms larger than L2 across a step"},
+        "roofline": {"bound": "hbm", "kernel": W["kernels"][dom], "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_source": peak_src, "algorithmic_bytes_per_call": k_bytes,
+                     "call_ms": round(k_ms, 4), "traffic": None,
+                     "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4)},
+        "gpu_launches": int(launches),
+        "e2e": None,
+        "clocks": clk.summary(),
+    }
+    if cpu_line is not None:
+        line["cpu_baseline"] = cpu_line
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_config_reference(args):
+    import torch
+    W = WORKLOADS[args.config]()
+    torch.set_num_threads(os.cpu_count() or 1)
+    times = []
+    steps, warmup = args.steps, args.warmup
+    for i in range(warmup + steps):
+        t = W["cpu"](W["cpu_rows"])
+        if i >= warmup:
+            times.append(t)
+        if t > 5.0:  # a heavy sample: keep the whole run within a few minutes
+            steps, warmup = min(steps, 2), min(warmup, i)
+            if len(times) >= steps:
+                break
+    tc = statistics.mean(times) if times else t
+    units = W.get("cpu_unit_per_row")
+    per = (W["cpu_rows"] * units) if units else W["per_step"] * W["cpu_rows"] / W["rows"]
+    value = per / tc / (1e9 if W["unit"] == "GB/s" else 1)
+    sample = (f"{W['cpu_rows']} {'batch entries' if units else 'rows'} per step through the fp64 "
+              f"CPU oracle port of the reference's CPU path (torch, {os.cpu_count()} threads)")
+    return {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": W["unit"],
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(tc * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic i.i.d. N(0,1)",
+            "config": {"workload": W["name"] + " (bounded sample)"},
+            "cpu_baseline": {"value": round(value, 4), "unit": W["unit"],
+                             "cores": os.cpu_count(), "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": W["unit"], "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=256)
+    ap.add_argument("--cpu-rows", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="cfg2, cfg3, cfg3l: rows per GPU (default: the config's; fewer for "
+                         "profiling)")
+    ap.add_argument("--config", default="cfg2", choices=["cfg2"] + sorted(WORKLOADS),
+                    help="cfg2 (default, the headline line) or another baseline config")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.config != "cfg2":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps(run_config_reference(args)), flush=True)
+            return 0
+        return run_config(args, rank, world, local_rank)
 
     if args.impl == "reference":
         if rank != 0:
