@@ -195,6 +195,7 @@ __device__ __forceinline__ void conv_one(const FwdParams<A>& f, const A* X, cons
     }
   }
   int pl = base - dil, pr = base + dil * P;
+#pragma unroll 8
   for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
 #pragma unroll
     for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
@@ -240,6 +241,7 @@ __device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab,
       }
     }
     int pl = base - dil, pr = base + dil * P;
+#pragma unroll 8
     for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
 #pragma unroll
       for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
@@ -263,20 +265,23 @@ __device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab,
 }
 
 // Per-row dL/dH of one scale: part[c*hcols + center + k] = sum_n gW_c(n) x_j(n - dil k) for
-// |k| <= K (zero elsewhere).  Warp w reduces taps [k0, k0 + KT) for kb = w, w + NW, ...; its
-// lanes split the positions (in phase-major order, so a window slides by one tap per step)
-// and are summed with shuffles.
+// |k| <= K (zero elsewhere).  Warp w reduces taps [k0, k0 + KT) for kb = w, w + NW, ...; its lanes
+// take runs of 8 positions n = nn + dil*t of one phase (runs ordered phase-minor, so that the
+// lanes of a warp read distinct banks), load the run's 15-value window of x_j and its 8 dL/dW
+// pairs once, and accumulate 8 x 8 packed products.  Positions past the row end read the zero
+// cells of the dL/dW buffer.  Lane partials are summed with shuffles.
 template <typename A, int C>
 __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, const A* gw,
                             A* part) {
+  static_assert(KT == 8, "a run is 8 positions");
   const int n = static_cast<int>(f.n);
   const int dil = O.dil, K = O.half;
+  const int lg = __ffs(dil) - 1;  // dil = 2^lg
   const int hcols = 2 * f.center + 1;
   const int ntap = 2 * K + 1;
   const int nkb = static_cast<int>(cdiv(ntap, KT));
   const int U = static_cast<int>(cdiv(n, dil));
-  const int tot = dil * U;
-  const int T = static_cast<int>(cdiv(tot, 32));
+  const int runs = dil * ((U + 7) >> 3);
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   using V2 = typename Cplx<A>::type;
   for (int c = threadIdx.x; c < C * hcols; c += NT) {
@@ -288,32 +293,21 @@ __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, con
     Acc2<A> acc[KT];
 #pragma unroll
     for (int i = 0; i < KT; ++i) acc[i].zero();
-    const int i0 = lane * T, i1 = min(tot, i0 + T);
-    if (i0 < i1) {
-      int phi = i0 / U, u = i0 - phi * U;
-      A win[KT];
-      bool fresh = true;
-      for (int idx = i0; idx < i1; ++idx) {
-        const int nn = phi + dil * u;
-        if (nn < n) {
-          if (fresh) {
+    for (int r = lane; r < runs; r += 32) {
+      const int nn = (r & (dil - 1)) + ((r >> lg) << (lg + 3));  // phase + dil * 8 * run
+      if (nn >= n) continue;
+      const int base = nn - dil * k0;
+      A xw[2 * KT - 1];  // x_j(base + dil*(m - 7)), m = 0..14
 #pragma unroll
-            for (int i = 0; i < KT; ++i) win[i] = ldE(f, X, nn - dil * (k0 + i));
-            fresh = false;
-          } else {
+      for (int m = 0; m < 2 * KT - 1; ++m) xw[m] = ldE(f, X, base + dil * (m - (KT - 1)));
 #pragma unroll
-            for (int i = KT - 1; i > 0; --i) win[i] = win[i - 1];
-            win[0] = ldE(f, X, nn - dil * k0);
-          }
-          const V2 gv = ld_gw<A, C>(gw, n, nn);
-          alignas(16) A gp[2] = {gv.x, gv.y};
+      for (int t = 0; t < KT; ++t) {
+        const V2 gv = ld_gw<A, C>(gw, n, nn + dil * t);
+        alignas(16) A gp[2] = {gv.x, gv.y};
 #pragma unroll
-          for (int i = 0; i < KT; ++i) acc[i].fma(gp, win[i], win[i]);
-        }
-        if (++u == U) {
-          u = 0;
-          ++phi;
-          fresh = true;
+        for (int i = 0; i < KT; ++i) {
+          const A xv = xw[t - i + KT - 1];  // x_j(nn + dil*t - dil*(k0 + i))
+          acc[i].fma(gp, xv, xv);
         }
       }
     }

@@ -236,6 +236,7 @@ __device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
   }
   int pl = phi + dil * (u0 - 1);          // next left load position
   int pr = phi + dil * (u0 + P);          // next right load position
+#pragma unroll 8
   for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
 #pragma unroll
     for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
