@@ -94,6 +94,28 @@ __device__ __forceinline__ typename Cplx<A>::type ld_gw(const A* gw, int n, int 
   }
   return v;
 }
+// The same without the clamp, for positions known to lie in [-1, n].
+template <typename A, int C>
+__device__ __forceinline__ typename Cplx<A>::type ld_gw_in(const A* gw, int pos) {
+  const int q = sidx<PS>(pos + 1);
+  typename Cplx<A>::type v;
+  if (C == 2) {
+    v = *reinterpret_cast<const typename Cplx<A>::type*>(gw + 2 * q);
+  } else {
+    v.x = gw[q];
+    v.y = A(0);
+  }
+  return v;
+}
+template <typename A, int C, bool CLAMP>
+__device__ __forceinline__ typename Cplx<A>::type ld_gw_sel(const A* gw, int n, int pos) {
+  return CLAMP ? ld_gw<A, C>(gw, n, pos) : ld_gw_in<A, C>(gw, pos);
+}
+template <typename A, bool CLAMP>
+__device__ __forceinline__ A ldE_sel(const FwdParams<A>& f, const A* buf, int pos) {
+  return CLAMP ? ldE(f, buf, pos) : buf[sidx<PS>(pos + f.ext)];
+}
+
 template <typename A, int C>
 __device__ __forceinline__ void st_gw(A* gw, int pos, A re, A im) {
   const int q = sidx<PS>(pos + 1);
@@ -213,7 +235,50 @@ __device__ __forceinline__ void conv_one(const FwdParams<A>& f, const A* X, cons
   }
 }
 
-// G(p) += sum_k h_re(k) gWre(p + dk) + h_im(k) gWim(p + dk) for p in [pa, pb).
+// Tap loop of one adjoint item: acc_i += sum_k (taps of k) . (R_i(k) +- conj L_i(k)), where
+// L_i(k) = gW(p_i - dk), R_i(k) = gW(p_i + dk).  In fp32 the complex sum and difference are one
+// packed FMA each: R + conj(L) = L * (1, -1) + R and R - conj(L) = L * (-1, 1) + R.
+template <typename A, int C, bool SYM, bool CLAMP>
+__device__ __forceinline__ void adjoint_taps(const A* tab, const A* gw, int n, int K, int dil,
+                                             int base, typename Cplx<A>::type (&L)[P],
+                                             typename Cplx<A>::type (&R)[P], Acc2<A> (&acc)[P]) {
+  int pl = base - dil, pr = base + dil * P;
+#pragma unroll 8
+  for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
+#pragma unroll
+    for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
+#pragma unroll
+    for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
+    L[0] = ld_gw_sel<A, C, CLAMP>(gw, n, pl);
+    R[P - 1] = ld_gw_sel<A, C, CLAMP>(gw, n, pr);
+    alignas(16) A t[4] = {tab[4 * k], tab[4 * k + 1], tab[4 * k + 2], tab[4 * k + 3]};
+    if constexpr (std::is_same<A, float>::value) {
+      const unsigned long long pm = pk(1.0f, -1.0f), mp = pk(-1.0f, 1.0f);
+      const unsigned long long t01 = pk(t[0], t[1]), t23 = pk(t[2], t[3]);
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const unsigned long long l = pk(L[i].x, L[i].y);
+        unsigned long long sd = pk(R[i].x, R[i].y);
+        ffma2(sd, l, pm);  // (Rre + Lre, Rim - Lim)
+        ffma2(acc[i].v, t01, sd);
+        if (!SYM) {
+          unsigned long long ds = pk(R[i].x, R[i].y);
+          ffma2(ds, l, mp);  // (Rre - Lre, Rim + Lim)
+          ffma2(acc[i].v, t23, ds);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        acc[i].fma(t, R[i].x + L[i].x, R[i].y - L[i].y);
+        if (!SYM) acc[i].fma(t + 2, R[i].x - L[i].x, R[i].y + L[i].y);
+      }
+    }
+  }
+}
+
+// G(p) += sum_k h_re(k) gWre(p + dk) + h_im(k) gWim(p + dk) for p in [pa, pb).  Items whose
+// whole window lies in [-1, n] skip the per-load clamp.
 template <typename A, int C, bool SYM>
 __device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab, const A* gw,
                               A* G, int pa, int pb) {
@@ -240,26 +305,35 @@ __device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab,
         acc[i].fma(t0, L[i].x, L[i].y);
       }
     }
-    int pl = base - dil, pr = base + dil * P;
-#pragma unroll 8
-    for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
-#pragma unroll
-      for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
-#pragma unroll
-      for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
-      L[0] = ld_gw<A, C>(gw, n, pl);
-      R[P - 1] = ld_gw<A, C>(gw, n, pr);
-      alignas(16) A t[4] = {tab[4 * k], tab[4 * k + 1], tab[4 * k + 2], tab[4 * k + 3]};
-#pragma unroll
-      for (int i = 0; i < P; ++i) {
-        acc[i].fma(t, R[i].x + L[i].x, R[i].y - L[i].y);
-        if (!SYM) acc[i].fma(t + 2, R[i].x - L[i].x, R[i].y + L[i].y);
-      }
-    }
+    if (base - dil * K >= -1 && base + dil * (P - 1 + K) <= n)
+      adjoint_taps<A, C, SYM, false>(tab, gw, n, K, dil, base, L, R, acc);
+    else
+      adjoint_taps<A, C, SYM, true>(tab, gw, n, K, dil, base, L, R, acc);
 #pragma unroll
     for (int i = 0; i < P; ++i) {
       const int q = base + dil * i;
       if (q < pb) atE(f, G, q) += acc[i].re() + acc[i].im();
+    }
+  }
+}
+
+// One run of gradh_scale: 8 positions nn + dil*t against the taps k0 .. k0 + 7 (base = nn - dil k0).
+template <typename A, int C, bool CLAMP>
+__device__ __forceinline__ void gradh_run(const FwdParams<A>& f, const A* X, const A* gw, int n,
+                                          int dil, int nn, int base, Acc2<A> (&acc)[KT]) {
+  using V2 = typename Cplx<A>::type;
+  A xw[2 * KT - 1];  // x_j(base + dil*(m - 7)), m = 0..14
+#pragma unroll
+  for (int m = 0; m < 2 * KT - 1; ++m)
+    xw[m] = ldE_sel<A, CLAMP>(f, X, base + dil * (m - (KT - 1)));
+#pragma unroll
+  for (int t = 0; t < KT; ++t) {
+    const V2 gv = ld_gw_sel<A, C, CLAMP>(gw, n, nn + dil * t);
+    alignas(16) A gp[2] = {gv.x, gv.y};
+#pragma unroll
+    for (int i = 0; i < KT; ++i) {
+      const A xv = xw[t - i + KT - 1];  // x_j(nn + dil*t - dil*(k0 + i))
+      acc[i].fma(gp, xv, xv);
     }
   }
 }
@@ -297,19 +371,10 @@ __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, con
       const int nn = (r & (dil - 1)) + ((r >> lg) << (lg + 3));  // phase + dil * 8 * run
       if (nn >= n) continue;
       const int base = nn - dil * k0;
-      A xw[2 * KT - 1];  // x_j(base + dil*(m - 7)), m = 0..14
-#pragma unroll
-      for (int m = 0; m < 2 * KT - 1; ++m) xw[m] = ldE(f, X, base + dil * (m - (KT - 1)));
-#pragma unroll
-      for (int t = 0; t < KT; ++t) {
-        const V2 gv = ld_gw<A, C>(gw, n, nn + dil * t);
-        alignas(16) A gp[2] = {gv.x, gv.y};
-#pragma unroll
-        for (int i = 0; i < KT; ++i) {
-          const A xv = xw[t - i + KT - 1];  // x_j(nn + dil*t - dil*(k0 + i))
-          acc[i].fma(gp, xv, xv);
-        }
-      }
+      const bool inside = base - dil * (KT - 1) >= -f.ext &&
+                          base + dil * (KT - 1) <= n + f.ext - 1 && nn + dil * (KT - 1) <= n;
+      if (inside) gradh_run<A, C, false>(f, X, gw, n, dil, nn, base, acc);
+      else gradh_run<A, C, true>(f, X, gw, n, dil, nn, base, acc);
     }
 #pragma unroll
     for (int i = 0; i < KT; ++i) {

@@ -962,12 +962,9 @@ int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
   const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
   if (!ANALYSIS) {
     // independent output tiles when their staging fits; the cluster kernel otherwise
-    const int ts = run_syn_tiles<T, LM>(rows, src0, lv, dst_final, h0, h1, L, off, stream,
-                                        ws_needed != nullptr);
-    if (ts != FDWT_ERR_UNSUPPORTED) {
-      if (ws_needed) *ws_needed = 0;
-      return ts;
-    }
+    const int ts = run_syn_tiles<T, LM>(rows, src0, lv, dst_final, h0, h1, L, off, ws,
+                                        ws_bytes, stream, ws_needed);
+    if (ts != FDWT_ERR_UNSUPPORTED) return ts;
   }
   if (!ANALYSIS) {
     for (auto& l : lv) {

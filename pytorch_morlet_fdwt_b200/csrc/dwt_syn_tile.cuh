@@ -550,12 +550,12 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
 
 // ------------------------------------------------------------------------------ host
 
-// Plans and launches the tile synthesis; FDWT_ERR_UNSUPPORTED when it does not apply (the
-// caller then uses the cluster kernel).  lv is in processing order (coarsest first).
+// Plans and launches the tile synthesis of the levels lv (processing order, coarsest first);
+// FDWT_ERR_UNSUPPORTED when it does not apply (the caller then uses the cluster kernel).
 template <typename T, int LM>
-int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
-                  const double* h0, const double* h1, int L, int off, cudaStream_t stream,
-                  bool dry_run) {
+int run_syn_tile_launch(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
+                        const double* h0, const double* h1, int L, int off, cudaStream_t stream,
+                        bool dry_run) {
   using A = typename AccOf<T>::type;
   const int J = static_cast<int>(lv.size());
   if (J < 1 || J > kMaxLevels) return FDWT_ERR_UNSUPPORTED;
@@ -649,6 +649,60 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
   if (st != FDWT_OK) return st;
   kern<<<static_cast<unsigned>(rows * p.tiles), TNT, smem, stream>>>(p);
   return launch_status();
+}
+
+}  // namespace dwtk
+}  // namespace fdwt
+
+namespace fdwt {
+namespace dwtk {
+
+// Every tile recomputes the cone of every level, so a deep transform of a long row pays the
+// per-level cost tiles x levels times.  Deep fp32 / fp64 syntheses of long rows are therefore
+// split: the coarse levels run first as their own (shorter-row, fewer-tile) synthesis that
+// writes its approximation to the workspace, and the last kSplitLevels levels read it from
+// there (one extra write and read of that approximation).  Returns the workspace it needs
+// through ws_needed when asked.
+constexpr int kSplitLevels = 3;
+
+template <typename T, int LM>
+int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
+                  const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
+                  cudaStream_t stream, size_t* ws_needed) {
+  using A = typename AccOf<T>::type;
+  const int J = static_cast<int>(lv.size());
+  const int64_t n0 = J > 0 ? lv[J - 1].n_in : 0;
+  const int T_tile = sizeof(A) == 8 ? 2048 : 4096;
+  const bool split = std::is_same<T, A>::value && J > kSplitLevels + 1 &&
+                     n0 >= 8 * static_cast<int64_t>(T_tile);
+  if (!split) {
+    const int st = run_syn_tile_launch<T, LM>(rows, a, lv, y, h0, h1, L, off, stream,
+                                              ws_needed != nullptr);
+    if (st == FDWT_OK && ws_needed) *ws_needed = 0;
+    return st;
+  }
+  // coarse part: levels lv[0 .. J-1-kSplitLevels], output = approximation of length m
+  const std::vector<Level> coarse(lv.begin(), lv.end() - kSplitLevels);
+  const std::vector<Level> fine(lv.end() - kSplitLevels, lv.end());
+  const int64_t m = coarse.back().n_in;
+  size_t inner = 0;
+  int st = run_syn_tiles<T, LM>(rows, a, coarse, nullptr, h0, h1, L, off, nullptr, 0, stream,
+                                &inner);
+  if (st != FDWT_OK) return st;
+  st = run_syn_tile_launch<T, LM>(rows, nullptr, fine, nullptr, h0, h1, L, off, stream, true);
+  if (st != FDWT_OK) return st;
+  const size_t mid = (static_cast<size_t>(rows) * m * sizeof(T) + 255) & ~size_t(255);
+  if (ws_needed) {
+    *ws_needed = mid + inner;
+    return FDWT_OK;
+  }
+  if (rows == 0) return FDWT_OK;
+  if (ws == nullptr || ws_bytes < mid + inner) return FDWT_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  st = run_syn_tiles<T, LM>(rows, a, coarse, w, h0, h1, L, off, w + mid, ws_bytes - mid, stream,
+                            nullptr);
+  if (st != FDWT_OK) return st;
+  return run_syn_tile_launch<T, LM>(rows, w, fine, y, h0, h1, L, off, stream, false);
 }
 
 }  // namespace dwtk
