@@ -674,7 +674,7 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
   const int64_t n0 = J > 0 ? lv[J - 1].n_in : 0;
   const int T_tile = sizeof(A) == 8 ? 2048 : 4096;
   const bool split = std::is_same<T, A>::value && J > kSplitLevels + 1 &&
-                     n0 >= 8 * static_cast<int64_t>(T_tile);
+                     n0 >= 2 * static_cast<int64_t>(T_tile);
   if (!split) {
     const int st = run_syn_tile_launch<T, LM>(rows, a, lv, y, h0, h1, L, off, stream,
                                               ws_needed != nullptr);
