@@ -171,9 +171,10 @@ __device__ void bwd_lowpass(const FwdParams<A>& f, const A* cur, A* nxt, int dil
     A v = A(0);
     if (q >= -live && q < n + live) {
       v = f.lpp[0] * ldE(f, cur, q);
-      for (int t = 1; t <= f.c_lp; ++t) {
-        v = fma(f.lpp[t], ldE(f, cur, q - dil * t), v);
-        v = fma(f.lpm[t], ldE(f, cur, q + dil * t), v);
+      for (int i = 0; i < f.n_lp; ++i) {
+        const int t = f.lp_t[i];
+        v = fma(f.lp_p[i], ldE(f, cur, q - dil * t), v);
+        v = fma(f.lp_m[i], ldE(f, cur, q + dil * t), v);
       }
     }
     atE(f, nxt, q) = v;
@@ -190,9 +191,10 @@ __device__ void bwd_lowpass_adjoint(const FwdParams<A>& f, const A* src, A* dst,
     A v = A(0);
     if (q >= -live && q < n + live) {
       v = f.lpp[0] * ldE(f, src, q);
-      for (int t = 1; t <= f.c_lp; ++t) {
-        v = fma(f.lpp[t], ldE(f, src, q + dil * t), v);
-        v = fma(f.lpm[t], ldE(f, src, q - dil * t), v);
+      for (int i = 0; i < f.n_lp; ++i) {
+        const int t = f.lp_t[i];
+        v = fma(f.lp_p[i], ldE(f, src, q + dil * t), v);
+        v = fma(f.lp_m[i], ldE(f, src, q - dil * t), v);
       }
     }
     atE(f, dst, q) = v;

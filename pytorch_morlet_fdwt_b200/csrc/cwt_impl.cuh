@@ -27,6 +27,7 @@
 #pragma once
 
 #include <algorithm>
+#include <cmath>
 #include <type_traits>
 #include <vector>
 
@@ -70,6 +71,12 @@ struct FwdParams {
   A inv_tau;
   A lpp[kMaxC + 1];  // lowpass[c_lp + t]
   A lpm[kMaxC + 1];  // lowpass[c_lp - t]
+  // the half-band taps that matter: offsets t >= 1 whose coefficient is not negligible (the
+  // even-offset taps of a half-band filter are zero up to rounding, ~1e-17 of the centre), with
+  // (lpp, lpm) for each; lp_sym when every kept pair is equal (x(q-dt) + x(q+dt) once)
+  int32_t n_lp, lp_sym;
+  int32_t lp_t[kMaxC];
+  A lp_p[kMaxC], lp_m[kMaxC];
   Oct oct[kMaxOct];
   int32_t order[kMaxScales];
   int32_t support[kMaxScales];
@@ -280,15 +287,34 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
     const int gs = p.order[O.begin + s0 + s];
     if (EPI == EPI_STORE) {
       A* yb = static_cast<A*>(p.y) + ((row * p.n_scales + gs) * n) * C;
+      const int64_t n0 = phi + static_cast<int64_t>(dil) * u0;
+      if (C == 2 && dil == 1 && n0 + P <= n &&
+          (reinterpret_cast<uintptr_t>(yb + 2 * n0) & 15) == 0) {
+        // 8 consecutive complex outputs: whole 16-byte vectors
+        if constexpr (std::is_same<A, float>::value) {
+          float4* d = reinterpret_cast<float4*>(yb + 2 * n0);
 #pragma unroll
-      for (int i = 0; i < P; ++i) {
-        const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
-        if (ni < n) {
-          if (C == 2) {
-            yb[2 * ni] = acc[s][i].re();
-            yb[2 * ni + 1] = acc[s][i].im();
-          } else {
-            yb[ni] = acc[s][i].re();
+          for (int i = 0; i < P; i += 2)
+            d[i / 2] = make_float4(acc[s][i].re(), acc[s][i].im(), acc[s][i + 1].re(),
+                                   acc[s][i + 1].im());
+        } else {
+          double2* d = reinterpret_cast<double2*>(yb + 2 * n0);
+#pragma unroll
+          for (int i = 0; i < P; ++i) d[i] = make_double2(acc[s][i].re(), acc[s][i].im());
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
+          if (ni < n) {
+            if (C == 2) {
+              typename std::conditional<std::is_same<A, float>::value, float2, double2>::type v;
+              v.x = acc[s][i].re();
+              v.y = acc[s][i].im();
+              *reinterpret_cast<decltype(v)*>(yb + 2 * ni) = v;
+            } else {
+              yb[ni] = acc[s][i].re();
+            }
           }
         }
       }
@@ -352,14 +378,22 @@ template <typename A>
 __device__ void lowpass_step(const FwdParams<A>& p, const A* cur, A* nxt, int dil, int live) {
   const int n = static_cast<int>(p.n);
   const int ext = p.ext;
-  const int c = p.c_lp;
   for (int q = threadIdx.x - ext; q < n + ext; q += NT) {
     A v = A(0);
     if (q >= -live && q < n + live) {
       v = p.lpp[0] * cur[sidx<PS>(q + ext)];
-      for (int t = 1; t <= c; ++t) {
-        v = fma(p.lpp[t], cur[sidx<PS>(q - dil * t + ext)], v);
-        v = fma(p.lpm[t], cur[sidx<PS>(q + dil * t + ext)], v);
+      if (p.lp_sym) {
+        for (int i = 0; i < p.n_lp; ++i) {
+          const int t = p.lp_t[i];
+          v = fma(p.lp_p[i], cur[sidx<PS>(q - dil * t + ext)] + cur[sidx<PS>(q + dil * t + ext)],
+                  v);
+        }
+      } else {
+        for (int i = 0; i < p.n_lp; ++i) {
+          const int t = p.lp_t[i];
+          v = fma(p.lp_p[i], cur[sidx<PS>(q - dil * t + ext)], v);
+          v = fma(p.lp_m[i], cur[sidx<PS>(q + dil * t + ext)], v);
+        }
       }
     }
     nxt[sidx<PS>(q + ext)] = v;
@@ -367,7 +401,7 @@ __device__ void lowpass_step(const FwdParams<A>& p, const A* cur, A* nxt, int di
 }
 
 template <typename T, typename A, int EPI>
-__global__ void __launch_bounds__(NT)
+__global__ void __launch_bounds__(NT, (sizeof(A) == 4 && EPI == EPI_STORE) ? 2 : 1)
 cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   extern __shared__ __align__(16) unsigned char smem[];
   A* buf0 = reinterpret_cast<A*>(smem);
@@ -546,9 +580,23 @@ void fill_common(FwdParams<A>& p, const fdwt_morlet_plan* pl, const Geometry& g,
   p.center = pl->center;
   p.c_lp = pl->c_lp;
   p.ext = g.ext;
+  double lp_max = 0.0;
+  for (int t = 0; t <= 2 * pl->c_lp; ++t) lp_max = std::max(lp_max, std::fabs(pl->lowpass[t]));
+  p.n_lp = 0;
+  p.lp_sym = 1;
   for (int t = 0; t <= kMaxC; ++t) {
     p.lpp[t] = t <= pl->c_lp ? static_cast<A>(pl->lowpass[pl->c_lp + t]) : A(0);
     p.lpm[t] = t <= pl->c_lp ? static_cast<A>(pl->lowpass[pl->c_lp - t]) : A(0);
+    if (t >= 1 && t <= pl->c_lp) {
+      const double a = pl->lowpass[pl->c_lp + t], b = pl->lowpass[pl->c_lp - t];
+      if (std::fabs(a) > 1e-13 * lp_max || std::fabs(b) > 1e-13 * lp_max) {
+        p.lp_t[p.n_lp] = t;
+        p.lp_p[p.n_lp] = static_cast<A>(a);
+        p.lp_m[p.n_lp] = static_cast<A>(b);
+        if (a != b) p.lp_sym = 0;
+        ++p.n_lp;
+      }
+    }
   }
   for (int j = 0; j < pl->n_octaves; ++j) {
     p.oct[j].dil = 1 << j;
