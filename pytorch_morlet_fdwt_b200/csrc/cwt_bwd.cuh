@@ -142,24 +142,50 @@ __device__ __forceinline__ A block_sum(A v, A* red) {
   return s;  // valid in thread 0
 }
 
-// Folded taps of one scale (k = 0..K), as in the forward's coefficient table; returns whether
-// the antisymmetric-real / symmetric-imaginary halves are all zero (exactly symmetric filter).
+// Folded taps of every scale of an octave (k = 0..K), as in the forward's coefficient table:
+// tab[(s * (K + 1) + k) * 4 + c]; sym[s] = 1 when the scale's antisymmetric-real /
+// symmetric-imaginary halves are all zero (exactly symmetric filter).  Ends with a barrier.
 template <typename A>
-__device__ bool build_scale_taps(const FwdParams<A>& f, const Oct& O, int s, A* tab, int* flag) {
-  if (threadIdx.x == 0) *flag = 0;
+__device__ void build_octave_taps(const FwdParams<A>& f, const Oct& O, A* tab, int* sym) {
+  const int K1 = O.half + 1;
+  for (int s = threadIdx.x; s < O.count; s += NT) sym[s] = 1;
   __syncthreads();
-  for (int k = threadIdx.x; k <= O.half; k += NT) {
+  for (int w = threadIdx.x; w < O.count * K1; w += NT) {
+    const int s = w / K1, k = w - s * K1;
     A t[4];
     fold_coef<A>(f, O, s, k, t);
-    tab[4 * k + 0] = t[0];
-    tab[4 * k + 1] = t[1];
-    tab[4 * k + 2] = t[2];
-    tab[4 * k + 3] = t[3];
-    if (t[2] != A(0) || t[3] != A(0)) atomicOr(flag, 1);
+    A* d = tab + 4 * w;
+    d[0] = t[0];
+    d[1] = t[1];
+    d[2] = t[2];
+    d[3] = t[3];
+    if (t[2] != A(0) || t[3] != A(0)) sym[s] = 0;
   }
   __syncthreads();
-  return *flag == 0;
 }
+
+// dL/dW of scale gs of the row (caller's gradient, (rows, S, n, C)) into a dL/dW buffer,
+// asynchronously (cp.async; the caller commits and waits).
+template <typename A, int C>
+__device__ __forceinline__ void stage_gw(const BwdParams<A>& p, int gs, int64_t row, A* gw) {
+  const int n = static_cast<int>(p.f.n);
+  const A* g = p.g + (row * p.f.n_scales + gs) * p.f.n * C;
+  constexpr int bytes = static_cast<int>(sizeof(A)) * C;
+  for (int q = threadIdx.x; q < n; q += NT) {
+    A* d = C == 2 ? gw + 2 * sidx<PS>(q + 1) : gw + sidx<PS>(q + 1);
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(d));
+    const A* src = g + static_cast<int64_t>(q) * C;
+    if (bytes == 16)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(src) : "memory");
+    else if (bytes == 8)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(src) : "memory");
+    else
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(src) : "memory");
+  }
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
 // ------------------------------------------------------------------------------ pyramid
 
@@ -473,6 +499,24 @@ __device__ void make_gw(const BwdParams<A>& p, const Oct& O, int s, int gs, cons
   }
 }
 
+// The gradient work of one scale whose dL/dW is in gw (barrier-separated from the producer):
+// its adjoint into G and its filter-gradient partial.
+template <typename A, int C, bool SYM>
+__device__ __forceinline__ void scale_grads(const BwdParams<A>& p, const Oct& O, int live, int gs,
+                                            A* G, const A* X, const A* gw, const A* tab,
+                                            int64_t row) {
+  const FwdParams<A>& f = p.f;
+  if (p.need_gx) {
+    const int reach = min(live, O.half * O.dil);
+    adjoint_scale<A, C, SYM>(f, O, tab, gw, G, -reach, static_cast<int>(f.n) + reach);
+  }
+  if (p.gh_part) {
+    const int hcols = 2 * f.center + 1;
+    gradh_scale<A, C>(f, O, X, gw, p.gh_part + (row * f.n_scales + gs) * C * hcols);
+  }
+}
+
+// MIX / SOFTMAX: dL/dW of each scale is formed from the recomputed W (make_gw) into one buffer.
 template <typename A, int EPI, int C, bool SYM>
 __device__ void scale_pass(const BwdParams<A>& p, const Oct& O, int live, int s, A* G,
                            const A* X, A* gw, const A* tab, A* red, int64_t row) {
@@ -492,24 +536,36 @@ __device__ void scale_pass(const BwdParams<A>& p, const Oct& O, int live, int s,
     if (threadIdx.x == 0) p.v_part[row * f.n_scales + gs] = ta;
   }
   __syncthreads();
-  if (p.need_gx) {
-    const int reach = min(live, O.half * O.dil);
-    adjoint_scale<A, C, SYM>(f, O, tab, gw, G, -reach, static_cast<int>(f.n) + reach);
-  }
-  if (p.gh_part) {
-    const int hcols = 2 * f.center + 1;
-    gradh_scale<A, C>(f, O, X, gw, p.gh_part + (row * f.n_scales + gs) * C * hcols);
-  }
+  scale_grads<A, C, SYM>(p, O, live, gs, G, X, gw, tab, row);
   __syncthreads();
 }
 
+// One octave.  STORE: the caller's dL/dW rows are double-buffered with cp.async, scale s + 1
+// loading while scale s is processed (the first one was issued by the caller).
 template <typename A, int EPI, int C>
 __device__ void octave_pass(const BwdParams<A>& p, const Oct& O, int live, A* G, const A* X,
-                            A* gw, A* tab, int* flag, A* red, int64_t row) {
+                            A* const* gws, const A* tab, const int* sym, A* red, int64_t row) {
+  const int K1 = O.half + 1;
   for (int s = 0; s < O.count; ++s) {
-    const bool sym = build_scale_taps<A>(p.f, O, s, tab, flag);
-    if (sym) scale_pass<A, EPI, C, true>(p, O, live, s, G, X, gw, tab, red, row);
-    else scale_pass<A, EPI, C, false>(p, O, live, s, G, X, gw, tab, red, row);
+    const A* ts = tab + 4 * K1 * s;
+    const bool sy = sym[s] != 0;
+    if (EPI == EPI_STORE) {
+      if (s + 1 < O.count) {
+        stage_gw<A, C>(p, p.f.order[O.begin + s + 1], row, gws[(s + 1) & 1]);
+        cp_commit();
+        cp_wait<1>();
+      } else {
+        cp_wait<0>();
+      }
+      __syncthreads();
+      const int gs = p.f.order[O.begin + s];
+      if (sy) scale_grads<A, C, true>(p, O, live, gs, G, X, gws[s & 1], ts, row);
+      else scale_grads<A, C, false>(p, O, live, gs, G, X, gws[s & 1], ts, row);
+      __syncthreads();
+    } else {
+      if (sy) scale_pass<A, EPI, C, true>(p, O, live, s, G, X, gws[0], ts, red, row);
+      else scale_pass<A, EPI, C, false>(p, O, live, s, G, X, gws[0], ts, red, row);
+    }
   }
 }
 
@@ -519,18 +575,20 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
   const FwdParams<A>& f = p.f;
   A* bufs[3] = {reinterpret_cast<A*>(smem), reinterpret_cast<A*>(smem) + f.buf_len,
                 reinterpret_cast<A*>(smem) + 2 * f.buf_len};
-  A* gw = reinterpret_cast<A*>(smem + p.gw_off);
+  A* gws[2] = {reinterpret_cast<A*>(smem + p.gw_off),
+               reinterpret_cast<A*>(smem + p.gw_off) + p.gw_len};
   A* tab = reinterpret_cast<A*>(smem + p.tab_off);
   A* red = reinterpret_cast<A*>(smem + p.red_off);
-  __shared__ int flag;
+  __shared__ int sym[kMaxScales];
   const int64_t row = blockIdx.x;
   const int n = static_cast<int>(f.n);
   const int E = f.ext;
   const int J = f.n_oct;
   const A* xr = static_cast<const A*>(f.x) + row * f.n;
 
-  // the end cells of the dL/dW buffer (positions -1 and n) are never written again
-  for (int q = threadIdx.x; q < p.gw_len; q += NT) gw[q] = A(0);
+  // the end cells of the dL/dW buffers (positions -1 and n) are never written again
+  for (int q = threadIdx.x; q < (EPI == EPI_STORE ? 2 : 1) * p.gw_len; q += NT) gws[0][q] = A(0);
+  __syncthreads();
 
   // pass 1: x_1 .. x_{J-1} into the row's scratch
   if (p.need_x && J > 1) {
@@ -569,6 +627,12 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
       G = Gn;
       Gn = t;
     }
+    if (O.count > 0 && EPI == EPI_STORE) {
+      // the octave's first dL/dW row loads while x_j and the taps are prepared
+      if (f.channels == 2) stage_gw<A, 2>(p, f.order[O.begin], row, gws[0]);
+      else stage_gw<A, 1>(p, f.order[O.begin], row, gws[0]);
+      cp_commit();
+    }
     if (O.count > 0) {
       if (p.need_x) {
         const int lv = O.live;
@@ -577,8 +641,9 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
           atE(f, X, q) = (q >= -lv && q < n + lv) ? srcp[q + lv] : A(0);
       }
       __syncthreads();
-      if (f.channels == 2) octave_pass<A, EPI, 2>(p, O, O.live, G, X, gw, tab, &flag, red, row);
-      else octave_pass<A, EPI, 1>(p, O, O.live, G, X, gw, tab, &flag, red, row);
+      build_octave_taps<A>(f, O, tab, sym);
+      if (f.channels == 2) octave_pass<A, EPI, 2>(p, O, O.live, G, X, gws, tab, sym, red, row);
+      else octave_pass<A, EPI, 1>(p, O, O.live, G, X, gws, tab, sym, red, row);
     }
   }
   __syncthreads();
@@ -772,10 +837,13 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   size_t off = 3 * static_cast<size_t>(p.f.buf_len) * sizeof(A);
   off = (off + 15) / 16 * 16;
   p.gw_off = static_cast<int>(off);
-  off += static_cast<size_t>(p.gw_len) * sizeof(A);
+  off += (EPI == EPI_STORE ? 2 : 1) * static_cast<size_t>(p.gw_len) * sizeof(A);
   off = (off + 15) / 16 * 16;
   p.tab_off = static_cast<int>(off);
-  off += 4 * (static_cast<size_t>(pl->center) + 1) * sizeof(A);
+  size_t tab = 0;  // the largest octave's tap tables
+  for (int j = 0; j < pl->n_octaves; ++j)
+    tab = std::max(tab, 4 * static_cast<size_t>(pl->oct_count[j]) * (pl->oct_half[j] + 1));
+  off += tab * sizeof(A);
   off = (off + 15) / 16 * 16;
   p.red_off = static_cast<int>(off);
   off += NW * sizeof(A);
