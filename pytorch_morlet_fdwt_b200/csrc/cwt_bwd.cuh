@@ -279,7 +279,7 @@ __device__ __forceinline__ void adjoint_taps(const A* tab, const A* gw, int n, i
     for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
     L[0] = ld_gw_sel<A, C, CLAMP>(gw, n, pl);
     R[P - 1] = ld_gw_sel<A, C, CLAMP>(gw, n, pr);
-    alignas(16) A t[4] = {tab[4 * k], tab[4 * k + 1], tab[4 * k + 2], tab[4 * k + 3]};
+    const A t[4] = {tab[4 * k], tab[4 * k + 1], tab[4 * k + 2], tab[4 * k + 3]};
     if constexpr (std::is_same<A, float>::value) {
       const unsigned long long pm = pk(1.0f, -1.0f), mp = pk(-1.0f, 1.0f);
       const unsigned long long t01 = pk(t[0], t[1]), t23 = pk(t[2], t[3]);
@@ -298,8 +298,8 @@ __device__ __forceinline__ void adjoint_taps(const A* tab, const A* gw, int n, i
     } else {
 #pragma unroll
       for (int i = 0; i < P; ++i) {
-        acc[i].fma(t, R[i].x + L[i].x, R[i].y - L[i].y);
-        if (!SYM) acc[i].fma(t + 2, R[i].x - L[i].x, R[i].y + L[i].y);
+        acc[i].fmav(t[0], t[1], R[i].x + L[i].x, R[i].y - L[i].y);
+        if (!SYM) acc[i].fmav(t[2], t[3], R[i].x - L[i].x, R[i].y + L[i].y);
       }
     }
   }
@@ -326,11 +326,11 @@ __device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab,
 #pragma unroll
     for (int i = 0; i < P; ++i) L[i] = R[i] = ld_gw<A, C>(gw, n, base + dil * i);
     {
-      alignas(16) A t0[2] = {tab[0], tab[3]};
+      const A t0 = tab[0], t3 = tab[3];
 #pragma unroll
       for (int i = 0; i < P; ++i) {
         acc[i].zero();
-        acc[i].fma(t0, L[i].x, L[i].y);
+        acc[i].fmav(t0, t3, L[i].x, L[i].y);
       }
     }
     if (base - dil * K >= -1 && base + dil * (P - 1 + K) <= n)
@@ -357,11 +357,10 @@ __device__ __forceinline__ void gradh_run(const FwdParams<A>& f, const A* X, con
 #pragma unroll
   for (int t = 0; t < KT; ++t) {
     const V2 gv = ld_gw_sel<A, C, CLAMP>(gw, n, nn + dil * t);
-    alignas(16) A gp[2] = {gv.x, gv.y};
 #pragma unroll
     for (int i = 0; i < KT; ++i) {
       const A xv = xw[t - i + KT - 1];  // x_j(nn + dil*t - dil*(k0 + i))
-      acc[i].fma(gp, xv, xv);
+      acc[i].fmav(gv.x, gv.y, xv, xv);
     }
   }
 }

@@ -110,6 +110,10 @@ struct Acc2<float> {
   __device__ __forceinline__ void fma(const float* c, float s0, float s1) {
     ffma2(v, *reinterpret_cast<const unsigned long long*>(c), pk(s0, s1));
   }
+  // the same with the coefficient pair by value (no addressable temporary)
+  __device__ __forceinline__ void fmav(float c0, float c1, float s0, float s1) {
+    ffma2(v, pk(c0, c1), pk(s0, s1));
+  }
   __device__ __forceinline__ float re() const { return lo_f(v); }
   __device__ __forceinline__ float im() const { return hi_f(v); }
 };
@@ -120,6 +124,10 @@ struct Acc2<double> {
   __device__ __forceinline__ void fma(const double* c, double s0, double s1) {
     r = ::fma(c[0], s0, r);
     i = ::fma(c[1], s1, i);
+  }
+  __device__ __forceinline__ void fmav(double c0, double c1, double s0, double s1) {
+    r = ::fma(c0, s0, r);
+    i = ::fma(c1, s1, i);
   }
   __device__ __forceinline__ double re() const { return r; }
   __device__ __forceinline__ double im() const { return i; }
