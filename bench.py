@@ -121,6 +121,21 @@ class ClockSampler:
                 "samples": len(self.samples), "reasons": sorted(self.reasons)}
 
 
+def max_over_ranks(values, world, device):
+    """Element-wise maximum of per-rank timings over all ranks (identity for one rank)."""
+    import torch
+    t = torch.tensor([float(v) for v in values], device=device, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.cpu()]
+
+
+def job_throughput(units_per_rank_step, steps, world, ms, scale=1.0):
+    """Whole-job rate: the units every rank processed over the slowest rank's time."""
+    return units_per_rank_step * steps * world / (ms / 1e3) / scale
+
+
 # ------------------------------------------------------------------------------ workload
 
 CFG2 = dict(shape=(16, 128, 65536), wavelet="db8", mode="periodization", level=8)
@@ -248,10 +263,7 @@ def run_ours(args, rank, world, local_rank, pool):
     ms = start.elapsed_time(end)
     ana_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ka, kb))
     syn_ms = statistics.mean(b.elapsed_time(c) for b, c in zip(kb, kc))
-    t = torch.tensor([ms, ana_ms, syn_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ana_ms, syn_ms = float(t[0]), float(t[1]), float(t[2])
+    ms, ana_ms, syn_ms = max_over_ranks([ms, ana_ms, syn_ms], world, dev)
 
     # end to end through the public API with host buffers (pinned), every step
     e2e_steps = max(1, min(args.steps, 10))
@@ -281,10 +293,7 @@ def run_ours(args, rank, world, local_rank, pool):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    te = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te[0])
+    (e2e_ms,) = max_over_ranks([e2e_ms], world, dev)
     return _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms,
                         launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
 
@@ -294,7 +303,7 @@ def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, sy
     if rank != 0:
         return None
     peak, peak_src = peaks()
-    value = step_bytes * args.steps * world / (ms / 1e3) / 1e9
+    value = job_throughput(step_bytes, args.steps, world, ms, 1e9)
     kernels = {
         "dwt_analysis_kernel<float,16>": ana_ms,
         "dwt_syn_tile_kernel<float,16,0>": syn_ms,
@@ -629,15 +638,13 @@ def run_config(args, rank, world, local_rank):
     ms = ev[0][0].elapsed_time(ev[-1][2])
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
-    t = torch.tensor([ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    ms, fwd_ms, bwd_ms = max_over_ranks([ms, fwd_ms, bwd_ms], world, dev)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.destroy_process_group()
-    ms, fwd_ms, bwd_ms = (float(v) for v in t)
     if rank != 0:
         return 0
     scale = 1e9 if W["unit"] == "GB/s" else 1.0
-    value = W["per_step"] * args.steps * world / (ms / 1e3) / scale
+    value = job_throughput(W["per_step"], args.steps, world, ms, scale)
     peak, peak_src = peaks()
     dom = 0 if fwd_ms >= bwd_ms or W["bwd_bytes"] == 0 else 1
     k_ms = fwd_ms if dom == 0 else bwd_ms
