@@ -52,6 +52,13 @@ int fdwt_last_cuda_error(void);
 int fdwt_version(void);
 /* Number of kernels this library has launched in the process (all threads, all devices). */
 unsigned long long fdwt_launch_count(void);
+/* Test hook.  While enabled (enable != 0), every kernel launch of this library is preceded,
+ * on the same stream, by a kernel that sets every shared-memory word of every SM to the 32-bit
+ * pattern `word` (e.g. a NaN or infinity bit pattern).  Shared memory is not cleared between
+ * kernels, so a kernel that reads a cell it has not written then sees that pattern: tests use
+ * this to check that no output depends on uninitialised shared memory.  Process-wide; the fill
+ * kernels are not counted by fdwt_launch_count(). */
+void fdwt_set_shared_memory_fill(int enable, unsigned int word);
 
 /* ------------------------------------------------------------------------------------------
  * Discrete wavelet transform.  One call runs every level of a multilevel transform (the

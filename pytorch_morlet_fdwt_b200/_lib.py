@@ -28,6 +28,7 @@ SIGNATURES = {
     "fdwt_last_cuda_error": (ctypes.c_int, []),
     "fdwt_version": (ctypes.c_int, []),
     "fdwt_launch_count": (ctypes.c_ulonglong, []),
+    "fdwt_set_shared_memory_fill": (None, [ctypes.c_int, ctypes.c_uint]),
     "fdwt_dwt_analysis": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, c_i64p, c_i64p,
         c_voidpp, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -158,3 +159,9 @@ def workspace(nbytes: int, device: torch.device):
 def launch_count() -> int:
     """Kernels launched by libfdwt_b200.so so far in this process."""
     return int(load().fdwt_launch_count())
+
+
+def set_shared_memory_fill(enable: bool, word: int = 0) -> None:
+    """Test hook: while enabled, every kernel of the library is preceded by one that sets all
+    shared memory to the 32-bit pattern `word` (see fdwt_set_shared_memory_fill)."""
+    load().fdwt_set_shared_memory_fill(1 if enable else 0, word & 0xFFFFFFFF)

@@ -77,3 +77,36 @@ extern "C" int fdwt_version(void) { return 100; }
 extern "C" unsigned long long fdwt_launch_count(void) {
   return fdwt::g_launches.load(std::memory_order_relaxed);
 }
+
+namespace {
+// One CTA per SM at the largest dynamic shared-memory size, every word set to `word`.
+__global__ void fill_shared_kernel(unsigned word, int words) {
+  extern __shared__ unsigned fill_smem[];
+  volatile unsigned* s = fill_smem;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) s[i] = word;
+}
+std::atomic<int> g_fill_enabled{0};
+std::atomic<unsigned> g_fill_word{0u};
+}  // namespace
+
+namespace fdwt {
+int pre_launch(cudaStream_t stream) {
+  if (!g_fill_enabled.load(std::memory_order_relaxed)) return FDWT_OK;
+  const int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(fill_shared_kernel));
+  if (st != FDWT_OK) return st;
+  const int bytes = max_smem_optin();
+  fill_shared_kernel<<<2 * sm_count(), 1024, bytes, stream>>>(
+      g_fill_word.load(std::memory_order_relaxed), bytes / 4);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return FDWT_ERR_CUDA;
+  }
+  return FDWT_OK;
+}
+}  // namespace fdwt
+
+extern "C" void fdwt_set_shared_memory_fill(int enable, unsigned int word) {
+  g_fill_word.store(word, std::memory_order_relaxed);
+  g_fill_enabled.store(enable != 0, std::memory_order_relaxed);
+}

@@ -46,6 +46,9 @@ int sm_count();
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize = device opt-in limit), cached per
 // (kernel, device).
 int allow_max_dynamic_smem(const void* kernel);
+// Called before every kernel launch: runs the shared-memory fill kernel of the test hook
+// fdwt_set_shared_memory_fill when it is enabled (FDWT_OK and nothing otherwise).
+int pre_launch(cudaStream_t stream);
 
 // ------------------------------------------------------------------------------ types
 template <typename T> struct AccOf { using type = float; };

@@ -691,6 +691,8 @@ int reduce_rows(const A* part, int64_t rows, int64_t cols, int64_t D, A* out, A*
   const int64_t nch = reduce_chunks(rows, cols, D);
   const int64_t per_d = cdiv(rows, D);
   const dim3 block(256);
+  int st = pre_launch(stream);
+  if (st != FDWT_OK) return st;
   if (nch == 1) {
     reduce_rows_kernel<A><<<dim3(static_cast<unsigned>(cdiv(cols, 256)), static_cast<unsigned>(D), 1),
                             block, 0, stream>>>(part, rows, cols, D, per_d, 1, out);
@@ -700,8 +702,9 @@ int reduce_rows(const A* part, int64_t rows, int64_t cols, int64_t D, A* out, A*
   reduce_rows_kernel<A><<<dim3(static_cast<unsigned>(cdiv(cols, 256)), static_cast<unsigned>(D),
                                static_cast<unsigned>(nch)),
                           block, 0, stream>>>(part, rows, cols, D, per_chunk, nch, tmp);
-  int st = launch_status();
+  st = launch_status();
   if (st != FDWT_OK) return st;
+  if ((st = pre_launch(stream)) != FDWT_OK) return st;
   reduce_rows_kernel<A><<<dim3(static_cast<unsigned>(cdiv(cols, 256)), static_cast<unsigned>(D), 1),
                           block, 0, stream>>>(tmp, nch * D, cols, D, nch, 1, out);
   return launch_status();
@@ -853,6 +856,7 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   auto kern = cwt_backward_kernel<A, EPI>;
   st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
   if (st != FDWT_OK) return st;
+  if ((st = pre_launch(stream)) != FDWT_OK) return st;
   kern<<<static_cast<unsigned>(rows), NT, smem, stream>>>(p);
   if ((st = launch_status()) != FDWT_OK) return st;
   if (gh && (st = reduce_rows<A>(ghp, rows, ghcols, 1, static_cast<A*>(gh), tmp, stream)) != FDWT_OK)

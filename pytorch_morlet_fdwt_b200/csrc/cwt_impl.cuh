@@ -669,6 +669,7 @@ int run_forward(int64_t rows, int64_t n, const void* x, const void* h,
   auto kern = cwt_forward_kernel<T, A, EPI>;
   st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
   if (st != FDWT_OK) return st;
+  if ((st = pre_launch(stream)) != FDWT_OK) return st;
   kern<<<static_cast<unsigned>(rows), NT, smem, stream>>>(p);
   return launch_status();
 }

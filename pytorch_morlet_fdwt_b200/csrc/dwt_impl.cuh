@@ -933,6 +933,7 @@ template <typename K, typename P>
 int launch(K kern, const P& p, int64_t rows, int cs, size_t smem, cudaStream_t stream) {
   int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
   if (st != FDWT_OK) return st;
+  if ((st = pre_launch(stream)) != FDWT_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(rows * cs));
   cfg.blockDim = dim3(NT);

@@ -83,6 +83,7 @@ struct LevelInfo {
   int32_t dst_slot[kTileSegs], dst_org[kTileSegs];  // where level i-1 keeps each range
   int32_t zl_end[kTileSegs];                    // margin cells to zero: [0, zl_end) and
   int32_t zr_beg[kTileSegs], zr_end[kTileSegs]; // [zr_beg, zr_end) of each output segment
+                                                // (all of its storage outside the outputs)
 };
 
 // ------------------------------------------------------------------------------ planning
@@ -223,12 +224,12 @@ __device__ void plan_tile(const TileParams<A, LM>& p, int t, TileGeo* geo, Level
       I.src_org[s] = org[ss];
       I.dst_slot[s] = f_slot[s];
       I.dst_org[s] = porg[s];
-      // margins of the output segment that stand for coefficients outside [0, nc)
+      // every margin cell of the output segment is zeroed (see the kernel)
       const int s0 = ps[s] - porg[s];
       const bool live = lane > 0 && pl[s] > 0;
-      I.zl_end[s] = (live && ps[s] == 0) ? s0 : 0;
+      I.zl_end[s] = live ? s0 : 0;
       I.zr_beg[s] = s0 + pl[s];
-      I.zr_end[s] = (live && ps[s] + pl[s] == f_nc) ? f_cap[s] : 0;
+      I.zr_end[s] = live ? f_cap[s] : 0;
     }
     I.edge = edge && folds;
   }
@@ -467,9 +468,12 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
       }
       for (int k = threadIdx.x; k < 2 * LM; k += TNT) zadd[k] = A(0);
     }
-    // in the next level's buffer, margins that stand for coefficients outside [0, nc) must read
-    // as zero (other margin cells only feed outputs that are discarded); they are disjoint from
-    // the cells this level's jobs write
+    // in the next level's buffer, every margin cell around the segments this level writes is
+    // zeroed: cells that stand for coefficients outside [0, nc) must read as zero, and the
+    // others are read through the zero taps (h[-1], h[LM]) of output pairs with one kept and one
+    // discarded output, so they must hold a finite value (0 * inf or 0 * nan left in shared
+    // memory by an earlier kernel would be nan); they are disjoint from the cells this level's
+    // items write
 #pragma unroll
     for (int s = 0; s < kTileSegs; ++s) {
       A* b = anext + I.dst_slot[s];
@@ -647,6 +651,7 @@ int run_syn_tile_launch(int64_t rows, const void* a, const std::vector<Level>& l
   auto kern = c0 ? dwt_syn_tile_kernel<T, LM, 1> : dwt_syn_tile_kernel<T, LM, 0>;
   int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
   if (st != FDWT_OK) return st;
+  if ((st = pre_launch(stream)) != FDWT_OK) return st;
   kern<<<static_cast<unsigned>(rows * p.tiles), TNT, smem, stream>>>(p);
   return launch_status();
 }
