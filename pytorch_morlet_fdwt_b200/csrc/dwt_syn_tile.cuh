@@ -663,12 +663,17 @@ namespace fdwt {
 namespace dwtk {
 
 // Every tile recomputes the cone of every level, so a deep transform of a long row pays the
-// per-level cost tiles x levels times.  Deep fp32 / fp64 syntheses of long rows are therefore
-// split: the coarse levels run first as their own (shorter-row, fewer-tile) synthesis that
-// writes its approximation to the workspace, and the last kSplitLevels levels read it from
-// there (one extra write and read of that approximation).  Returns the workspace it needs
-// through ws_needed when asked.
-constexpr int kSplitLevels = 3;
+// per-level cost tiles x levels times, and every level of a tile is a barrier-separated step
+// with few warps per SM (the staging of all its levels limits the CTAs per SM).  Deep fp32 /
+// fp64 syntheses of long rows are therefore split: the coarse levels run first as their own
+// (shorter-row, fewer-tile) synthesis that writes its approximation to the workspace, and the
+// last kSplitLevels levels read it from there (one extra write and read of that
+// approximation).  The coarse part splits again while its rows are long, so a long row runs
+// its fine levels as one-level launches (small CTAs, many per SM, one barrier) and its coarse
+// levels together.  One level per fine launch was the fastest choice on B200 (db8, fp32 and
+// fp64, 16K..64K samples per row: 3-10% faster than two levels, 8-15% faster than three).
+// Returns the workspace it needs through ws_needed when asked.
+constexpr int kSplitLevels = 1;
 
 template <typename T, int LM>
 int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
@@ -676,38 +681,57 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
                   cudaStream_t stream, size_t* ws_needed) {
   using A = typename AccOf<T>::type;
   const int J = static_cast<int>(lv.size());
-  const int64_t n0 = J > 0 ? lv[J - 1].n_in : 0;
-  const int T_tile = sizeof(A) == 8 ? 2048 : 4096;
-  const bool split = std::is_same<T, A>::value && J > kSplitLevels + 1 &&
-                     n0 >= 2 * static_cast<int64_t>(T_tile);
-  if (!split) {
+  const int64_t T_tile = sizeof(A) == 8 ? 2048 : 4096;
+  // stages, coarsest first: levels [0, cut[0]) together, then kSplitLevels levels per stage;
+  // stage s (but the last) hands its approximation to stage s + 1 through the workspace
+  std::vector<int> cut;  // first level of each fine stage
+  int c = J;
+  while (std::is_same<T, A>::value && c > kSplitLevels + 1 && lv[c - 1].n_in >= 2 * T_tile)
+    c -= kSplitLevels;
+  if (c == J) {
     const int st = run_syn_tile_launch<T, LM>(rows, a, lv, y, h0, h1, L, off, stream,
                                               ws_needed != nullptr);
     if (st == FDWT_OK && ws_needed) *ws_needed = 0;
     return st;
   }
-  // coarse part: levels lv[0 .. J-1-kSplitLevels], output = approximation of length m
-  const std::vector<Level> coarse(lv.begin(), lv.end() - kSplitLevels);
-  const std::vector<Level> fine(lv.end() - kSplitLevels, lv.end());
-  const int64_t m = coarse.back().n_in;
-  size_t inner = 0;
-  int st = run_syn_tiles<T, LM>(rows, a, coarse, nullptr, h0, h1, L, off, nullptr, 0, stream,
-                                &inner);
-  if (st != FDWT_OK) return st;
-  st = run_syn_tile_launch<T, LM>(rows, nullptr, fine, nullptr, h0, h1, L, off, stream, true);
-  if (st != FDWT_OK) return st;
-  const size_t mid = (static_cast<size_t>(rows) * m * sizeof(T) + 255) & ~size_t(255);
+  for (int k = c; k < J; k += kSplitLevels) cut.push_back(k);
+  const int ns = static_cast<int>(cut.size()) + 1;
+  auto stage = [&](int s) {
+    const int b = s == 0 ? 0 : cut[s - 1];
+    const int e = s + 1 < ns ? cut[s] : J;
+    return std::vector<Level>(lv.begin() + b, lv.begin() + e);
+  };
+  // the approximation stage s hands over has lv[cut[s]].a_len = lv[cut[s] - 1].n_in samples
+  // per row; the stage outputs alternate between two regions, the last-but-one in region 0
+  size_t region[2] = {0, 0};
+  for (int s = 0; s + 1 < ns; ++s) {
+    const size_t bytes = (static_cast<size_t>(rows) * lv[cut[s] - 1].n_in * sizeof(T) + 255) &
+                         ~size_t(255);
+    size_t& r = region[(ns - 2 - s) & 1];
+    r = std::max(r, bytes);
+  }
+  for (int s = 0; s < ns; ++s) {  // every stage must be plannable before anything launches
+    const int st = run_syn_tile_launch<T, LM>(rows, nullptr, stage(s), nullptr, h0, h1, L, off,
+                                              stream, true);
+    if (st != FDWT_OK) return st;
+  }
   if (ws_needed) {
-    *ws_needed = mid + inner;
+    *ws_needed = region[0] + region[1];
     return FDWT_OK;
   }
   if (rows == 0) return FDWT_OK;
-  if (ws == nullptr || ws_bytes < mid + inner) return FDWT_ERR_WORKSPACE;
-  unsigned char* w = static_cast<unsigned char*>(ws);
-  st = run_syn_tiles<T, LM>(rows, a, coarse, w, h0, h1, L, off, w + mid, ws_bytes - mid, stream,
-                            nullptr);
-  if (st != FDWT_OK) return st;
-  return run_syn_tile_launch<T, LM>(rows, w, fine, y, h0, h1, L, off, stream, false);
+  if (ws == nullptr || ws_bytes < region[0] + region[1]) return FDWT_ERR_WORKSPACE;
+  unsigned char* base[2] = {static_cast<unsigned char*>(ws),
+                            static_cast<unsigned char*>(ws) + region[0]};
+  const void* src = a;
+  for (int s = 0; s < ns; ++s) {
+    void* dst = s + 1 < ns ? static_cast<void*>(base[(ns - 2 - s) & 1]) : y;
+    const int st = run_syn_tile_launch<T, LM>(rows, src, stage(s), dst, h0, h1, L, off, stream,
+                                              false);
+    if (st != FDWT_OK) return st;
+    src = dst;
+  }
+  return FDWT_OK;
 }
 
 }  // namespace dwtk
