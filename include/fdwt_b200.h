@@ -59,6 +59,11 @@ unsigned long long fdwt_launch_count(void);
  * this to check that no output depends on uninitialised shared memory.  Process-wide; the fill
  * kernels are not counted by fdwt_launch_count(). */
 void fdwt_set_shared_memory_fill(int enable, unsigned int word);
+/* Device-side error word of the current device: kernels that wait on asynchronous copies give
+ * up after a bounded number of tries, store a nonzero code there (1: a copy never completed)
+ * and return without finishing their work.  Synchronises the device, writes the code to
+ * *code (0: none since the last call) and clears it. */
+int fdwt_device_error(int* code);
 
 /* ------------------------------------------------------------------------------------------
  * Discrete wavelet transform.  One call runs every level of a multilevel transform (the

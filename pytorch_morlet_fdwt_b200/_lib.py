@@ -29,6 +29,7 @@ SIGNATURES = {
     "fdwt_version": (ctypes.c_int, []),
     "fdwt_launch_count": (ctypes.c_ulonglong, []),
     "fdwt_set_shared_memory_fill": (None, [ctypes.c_int, ctypes.c_uint]),
+    "fdwt_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "fdwt_dwt_analysis": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, c_i64p, c_i64p,
         c_voidpp, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -159,6 +160,14 @@ def workspace(nbytes: int, device: torch.device):
 def launch_count() -> int:
     """Kernels launched by libfdwt_b200.so so far in this process."""
     return int(load().fdwt_launch_count())
+
+
+def device_error() -> int:
+    """Read and clear the device-side error word (nonzero: a kernel gave up waiting on an
+    asynchronous copy and left its work unfinished)."""
+    v = ctypes.c_int(0)
+    check(load().fdwt_device_error(ctypes.byref(v)), "fdwt_device_error")
+    return int(v.value)
 
 
 def set_shared_memory_fill(enable: bool, word: int = 0) -> None:

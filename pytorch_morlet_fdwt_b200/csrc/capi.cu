@@ -106,6 +106,37 @@ int pre_launch(cudaStream_t stream) {
 }
 }  // namespace fdwt
 
+namespace {
+// Set (to a nonzero code) by a kernel whose bounded wait on an asynchronous copy ran out.
+__device__ int g_device_error;
+}  // namespace
+
+namespace fdwt {
+int* device_error_flag() {
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+}  // namespace fdwt
+
+extern "C" int fdwt_device_error(int* code) {
+  if (code == nullptr) return FDWT_ERR_INVALID;
+  int v = 0;
+  FDWT_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  if (v != 0) {
+    const int zero = 0;
+    FDWT_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  }
+  *code = v;
+  return FDWT_OK;
+}
+
 extern "C" void fdwt_set_shared_memory_fill(int enable, unsigned int word) {
   g_fill_word.store(word, std::memory_order_relaxed);
   g_fill_enabled.store(enable != 0, std::memory_order_relaxed);

@@ -49,6 +49,11 @@ int allow_max_dynamic_smem(const void* kernel);
 // Called before every kernel launch: runs the shared-memory fill kernel of the test hook
 // fdwt_set_shared_memory_fill when it is enabled (FDWT_OK and nothing otherwise).
 int pre_launch(cudaStream_t stream);
+// Device address of the current device's error word (0: no error).  A kernel whose bounded
+// wait on an asynchronous copy runs out stores a nonzero code there and returns early;
+// fdwt_device_error() reads and clears it.
+int* device_error_flag();
+constexpr int kErrCopyTimeout = 1;
 
 // ------------------------------------------------------------------------------ types
 template <typename T> struct AccOf { using type = float; };

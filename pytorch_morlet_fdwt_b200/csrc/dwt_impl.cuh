@@ -766,6 +766,7 @@ constexpr int kLM[] = {2, 4, 6, 8, 10, 12, 16, 20, 24, 32, 40, 64};
 }  // namespace fdwt
 
 #include "dwt_syn_tile.cuh"
+#include "dwt_stream.cuh"
 
 namespace fdwt {
 namespace dwtk {

@@ -38,6 +38,22 @@ constexpr int TQ = 4;        // output pairs per work item
 constexpr int TPS = 2;       // one pad element per 4 stored coefficients
 constexpr int kTileSegs = 3;
 
+// Outputs per tile of rows longer than about one tile (shorter rows are one tile).
+template <typename A>
+constexpr int tile_outputs() { return sizeof(A) == 8 ? 2048 : 4096; }
+
+// The streaming one-level synthesis (dwt_stream.cuh): filters up to kStreamMaxLM taps; a level
+// of a shape for which stream_fills() holds streams every tile down to kStreamMinOut outputs.
+constexpr int kStreamMaxLM = 24;
+constexpr int kStreamMinOut = 512;
+
+// One-level synthesis of this shape streams every tile: periodization over exactly one period
+// (n = 2 nc: a circular convolution of the coefficients) or zero mode (nothing folds back).
+inline bool stream_fills(const Level& l) {
+  return (l.mode == FDWT_MODE_PERIODIZATION && l.n_in == 2 * l.n_coef && l.P == l.n_in) ||
+         l.mode == FDWT_MODE_ZERO;
+}
+
 struct TileLevel {     // level i (0 = finest)
   int32_t n_out;       // output length (before the next level's trim)
   int32_t nc;          // coefficients
@@ -57,6 +73,9 @@ struct TileParams {
   int64_t a_stride;
   void* y;             // (rows, lv[0].n_out)
   int32_t J, off, T, W, tiles, ML;
+  int32_t run_tiles;    // tiles per row this launch runs: k < t_split is tile k, the others
+  int32_t t_split;      // tile k + t_skip (tiles [t_split, t_split + t_skip) run elsewhere)
+  int32_t t_skip;
   int32_t abuf_len[2]; // padded elements of the approximation buffers of even / odd levels
   int32_t d_len;       // padded elements of the d staging area
   int32_t origin_res;  // residue mod 4 of every segment origin
@@ -405,8 +424,9 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
   __shared__ A zl[2 * LM + 8], zr[2 * LM + 8];
   __shared__ A zadd[2 * LM];  // folded exterior values per edge-zone output (see zone_index)
 
-  const int64_t row = blockIdx.x / p.tiles;
-  const int t = static_cast<int>(blockIdx.x % p.tiles);
+  const int64_t row = blockIdx.x / p.run_tiles;
+  const int tk = static_cast<int>(blockIdx.x % p.run_tiles);
+  const int t = tk < p.t_split ? tk : tk + p.t_skip;
   const int J = p.J;
   if (threadIdx.x < 32) plan_tile<A, LM>(p, t, geo, info);
   __syncthreads();
@@ -556,10 +576,11 @@ dwt_syn_tile_kernel(const __grid_constant__ TileParams<typename AccOf<T>::type, 
 
 // Plans and launches the tile synthesis of the levels lv (processing order, coarsest first);
 // FDWT_ERR_UNSUPPORTED when it does not apply (the caller then uses the cluster kernel).
+// Tiles [skip_lo, skip_hi) of every row are left out (another kernel computes them).
 template <typename T, int LM>
 int run_syn_tile_launch(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
                         const double* h0, const double* h1, int L, int off, cudaStream_t stream,
-                        bool dry_run) {
+                        bool dry_run, int skip_lo = 0, int skip_hi = 0) {
   using A = typename AccOf<T>::type;
   const int J = static_cast<int>(lv.size());
   if (J < 1 || J > kMaxLevels) return FDWT_ERR_UNSUPPORTED;
@@ -577,11 +598,15 @@ int run_syn_tile_launch(int64_t rows, const void* a, const std::vector<Level>& l
   const int64_t n0 = lv[J - 1].n_in;
   for (const auto& l : lv)
     if (l.n_in > 0x3fffffffLL || l.a_len > 0x3fffffffLL) return FDWT_ERR_UNSUPPORTED;
-  int T_tile = sizeof(A) == 8 ? 2048 : 4096;
+  int T_tile = tile_outputs<A>();
   const int F0 = 4 * LM + 2 * p.W + 64;
   if (n0 <= T_tile + 2 * p.W) T_tile = static_cast<int>(n0);
   p.T = T_tile;
   p.tiles = static_cast<int>(cdiv(n0, T_tile));
+  if (skip_hi > skip_lo && (skip_lo < 0 || skip_hi > p.tiles)) return FDWT_ERR_INVALID;
+  p.t_split = skip_hi > skip_lo ? skip_lo : p.tiles;
+  p.t_skip = skip_hi > skip_lo ? skip_hi - skip_lo : 0;
+  p.run_tiles = p.tiles - p.t_skip;
   // bounds of the main ranges, fine to coarse, and the full / partial split
   std::vector<int64_t> mbound(J), cbound(J);
   int64_t mb = T_tile;
@@ -646,13 +671,14 @@ int run_syn_tile_launch(int64_t rows, const void* a, const std::vector<Level>& l
                         2 * (2 * LM + 8) * sizeof(A) - 2 * LM * sizeof(A);
   if (smem > budget) return FDWT_ERR_UNSUPPORTED;
   if (rows * p.tiles > 0x7fffffffLL) return FDWT_ERR_UNSUPPORTED;
+  if (p.run_tiles == 0) return FDWT_OK;
   if (dry_run || rows == 0) return FDWT_OK;
   const bool c0 = (off & 1) != 0;
   auto kern = c0 ? dwt_syn_tile_kernel<T, LM, 1> : dwt_syn_tile_kernel<T, LM, 0>;
   int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
   if (st != FDWT_OK) return st;
   if ((st = pre_launch(stream)) != FDWT_OK) return st;
-  kern<<<static_cast<unsigned>(rows * p.tiles), TNT, smem, stream>>>(p);
+  kern<<<static_cast<unsigned>(rows * p.run_tiles), TNT, smem, stream>>>(p);
   return launch_status();
 }
 
@@ -665,15 +691,31 @@ namespace dwtk {
 // Every tile recomputes the cone of every level, so a deep transform of a long row pays the
 // per-level cost tiles x levels times, and every level of a tile is a barrier-separated step
 // with few warps per SM (the staging of all its levels limits the CTAs per SM).  Deep fp32 /
-// fp64 syntheses of long rows are therefore split: the coarse levels run first as their own
+// fp64 syntheses are therefore split into stages: the coarse levels run first as their own
 // (shorter-row, fewer-tile) synthesis that writes its approximation to the workspace, and the
-// last kSplitLevels levels read it from there (one extra write and read of that
-// approximation).  The coarse part splits again while its rows are long, so a long row runs
-// its fine levels as one-level launches (small CTAs, many per SM, one barrier) and its coarse
-// levels together.  One level per fine launch was the fastest choice on B200 (db8, fp32 and
-// fp64, 16K..64K samples per row: 3-10% faster than two levels, 8-15% faster than three).
-// Returns the workspace it needs through ws_needed when asked.
+// finer levels run one per stage, reading the approximation of the stage before.  A level that
+// the streaming kernel (dwt_stream.cuh) can take whole -- periodization or zero mode, rows of a
+// multiple of 16 bytes, at least kStreamMinOut outputs -- runs alone; it then moves its bytes
+// near the copy bandwidth, which outweighs the extra write and read of the handed-over
+// approximation.  Other levels run alone while their rows are long (one-level tile launches
+// were 3-15% faster than two or three levels per launch on B200).  Returns the workspace it
+// needs through ws_needed when asked.
 constexpr int kSplitLevels = 1;
+
+template <typename T, int LM>
+int run_syn_stream(int64_t rows, const void* a, const Level& L0, void* y, const double* h0,
+                   const double* h1, int L, int off, cudaStream_t stream);
+
+// One stage: a one-level stage tries the streaming kernel (dwt_stream.cuh) first.
+template <typename T, int LM>
+int run_syn_stage(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
+                  const double* h0, const double* h1, int L, int off, cudaStream_t stream) {
+  if (lv.size() == 1) {
+    const int st = run_syn_stream<T, LM>(rows, a, lv[0], y, h0, h1, L, off, stream);
+    if (st != FDWT_ERR_UNSUPPORTED) return st;
+  }
+  return run_syn_tile_launch<T, LM>(rows, a, lv, y, h0, h1, L, off, stream, false);
+}
 
 template <typename T, int LM>
 int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
@@ -681,14 +723,25 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
                   cudaStream_t stream, size_t* ws_needed) {
   using A = typename AccOf<T>::type;
   const int J = static_cast<int>(lv.size());
-  const int64_t T_tile = sizeof(A) == 8 ? 2048 : 4096;
+  const int64_t T_tile = tile_outputs<A>();
   // stages, coarsest first: levels [0, cut[0]) together, then kSplitLevels levels per stage;
   // stage s (but the last) hands its approximation to stage s + 1 through the workspace
   std::vector<int> cut;  // first level of each fine stage
   int c = J;
-  while (std::is_same<T, A>::value && c > kSplitLevels + 1 && lv[c - 1].n_in >= 2 * T_tile)
+  while (std::is_same<T, A>::value && c > kSplitLevels) {
+    // a level that streams every tile (dwt_stream.cuh) runs alone down to short rows; the
+    // others while their rows are long
+    const Level& f = lv[c - 1];
+    constexpr int VW = 16 / static_cast<int>(sizeof(A));
+    const bool streams = stream_fills(f) && LM <= kStreamMaxLM && f.n_in >= kStreamMinOut &&
+                         f.n_in % VW == 0 && f.n_coef % VW == 0 && f.a_len % VW == 0;
+    const bool alone = streams || (c > kSplitLevels + 1 && f.n_in >= 2 * T_tile);
+    if (!alone) break;
     c -= kSplitLevels;
+  }
   if (c == J) {
+    if (ws_needed == nullptr && rows > 0)
+      return run_syn_stage<T, LM>(rows, a, lv, y, h0, h1, L, off, stream);
     const int st = run_syn_tile_launch<T, LM>(rows, a, lv, y, h0, h1, L, off, stream,
                                               ws_needed != nullptr);
     if (st == FDWT_OK && ws_needed) *ws_needed = 0;
@@ -726,8 +779,7 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
   const void* src = a;
   for (int s = 0; s < ns; ++s) {
     void* dst = s + 1 < ns ? static_cast<void*>(base[(ns - 2 - s) & 1]) : y;
-    const int st = run_syn_tile_launch<T, LM>(rows, src, stage(s), dst, h0, h1, L, off, stream,
-                                              false);
+    const int st = run_syn_stage<T, LM>(rows, src, stage(s), dst, h0, h1, L, off, stream);
     if (st != FDWT_OK) return st;
     src = dst;
   }

@@ -12,6 +12,7 @@ import torch
 from torch.autograd import gradcheck, gradgradcheck
 
 import pytorch_morlet_fdwt_b200 as F
+from pytorch_morlet_fdwt_b200 import _lib
 from oracle import dwt_oracle as D
 from tests.golden_data import bank_from_golden, golden
 
@@ -232,3 +233,34 @@ def test_empty_batch_and_noncontiguous():
     for c, r in zip(F.wavedec(xt, bank, "symmetric", 2),
                     D.wavedec(xt.cpu().numpy(), tb, "symmetric", 2)):
         close(c, r, 1e-12, 1.0)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.float64, 1e-12)])
+@pytest.mark.parametrize("wname,mode,nc", [("db8", "periodization", 32768), ("db4", "periodization", 16384),
+                                           ("haar", "periodization", 16384), ("db10", "periodization", 12288),
+                                           ("db12", "periodization", 12288), ("db3", "zero", 8196),
+                                           ("db4", "reflect", 8192), ("db20", "periodization", 16384)])
+def test_one_level_synthesis_long_rows(wname, mode, nc, dtype, tol):
+    """One-level syntheses of long rows: interior tiles on the streaming kernel (bulk copies
+    through an mbarrier ring; filters up to 24 taps, rows whose lengths are multiples of 16
+    bytes), the tiles near the row ends -- and every tile of db20 -- on the tile kernel.  Also
+    the same level as the last stage of a deeper waverec, and the device error word stays 0."""
+    torch.manual_seed(11)
+    bank = F.get_filter_bank(wname)
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    a = torch.randn(5, nc, dtype=dtype, device=DEV)
+    d = torch.randn(5, nc, dtype=dtype, device=DEV)
+    y = F.idwt(a, d, bank, mode)
+    close(y, D.idwt(a.double().cpu().numpy(), d.double().cpu().numpy(), tb, mode), tol)
+    ag, dg = a.clone().requires_grad_(), d.clone().requires_grad_()
+    gy = torch.randn_like(y)
+    (F.idwt(ag, dg, bank, mode) * gy).sum().backward()
+    ga, gd = D.idwt_vjp(gy.double().cpu().numpy(), nc, tb, mode)
+    close(ag.grad, ga, tol)
+    close(dg.grad, gd, tol)
+    x = torch.randn(3, y.shape[-1], dtype=dtype, device=DEV)
+    coeffs = F.wavedec(x, bank, mode, 3)
+    ref = D.wavedec(x.double().cpu().numpy(), tb, mode, 3)
+    close(F.waverec(coeffs, bank, mode), D.waverec(ref, tb, mode), tol)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
