@@ -5,11 +5,12 @@
 
 Default workload (configs[1] of the baseline, the one the headline metric is quoted on):
 db8 ``periodization`` level-8 ``wavedec`` of x float32 (16, 128, 65536) i.i.d. N(0,1), ``waverec``
-of the coefficients, and the autograd backward through both.  One step = those four fused
-launches over the whole batch; inputs (512 MiB per array) are larger than the 126 MB L2.
+of the coefficients, and the autograd backward through both.  One step = those four
+multilevel transforms over the whole batch (each a chain of one-level streaming launches);
+inputs (512 MiB per array) are larger than the 126 MB L2.
 
-``value`` is the whole-job algorithmic HBM throughput in GB/s (unique bytes read + written by
-the four launches: inputs once, outputs once), device-timed with CUDA events over K steps,
+``value`` is the whole-job algorithmic HBM throughput in GB/s (unique bytes the four transforms
+must read and write: inputs once, outputs once), device-timed with CUDA events over K steps,
 max over ranks.  Each rank runs the full config on its own data ("weak" scaling: the path
 shards by rows and has no collective).  ``e2e`` repeats the step through the public API with
 the input in pinned host memory and the gradient copied back every step.
@@ -38,12 +39,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "DWT/CWT achieved HBM GB/s (% of B200 peak); Morlet mixer tokens/s fwd+bwd"
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) per full-size launch, from one ncu capture of each kernel on 512 of
-# the 2048 rows scaled by 4 (traffic grows with the rows); the captures are summarised in
-# profiles/dwt_cfg2_kernels.txt (a text file, not this build's notes)
+# DRAM bytes (read + write) per full-size launch of the finest-level kernels, from one ncu
+# capture of each on 1024 of the 2048 rows scaled by 2 (traffic grows with the rows); the
+# captures are summarised in profiles/dwt_cfg2_kernels.txt
 TRAFFIC_PER_LAUNCH = {
-    "dwt_analysis_kernel<float,16>": 897_000_000,
-    "dwt_syn_tile_kernel<float,16,0>": 914_000_000,
+    "dwt_ana_stream_kernel<float,16>": 975_800_000,
+    "dwt_syn_stream_kernel<float,16,0>": 970_200_000,
 }
 
 
@@ -237,9 +238,8 @@ def run_ours(args, rank, world, local_rank, pool):
         step(x)
     torch.cuda.synchronize()
 
-    # per-launch device time of the two kernels of the step: the fused multilevel analysis
-    # (wavedec; also the waverec backward) and the tile synthesis (waverec; also the wavedec
-    # backward), each timed on its forward call
+    # device time of the two multilevel calls of the step (wavedec; also the waverec backward,
+    # and waverec; also the wavedec backward), each timed on its forward call
     ka, kb, kc = ([torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
                   for _ in range(3))
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -264,50 +264,113 @@ def run_ours(args, rank, world, local_rank, pool):
     ana_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ka, kb))
     syn_ms = statistics.mean(b.elapsed_time(c) for b, c in zip(kb, kc))
     ms, ana_ms, syn_ms = max_over_ranks([ms, ana_ms, syn_ms], world, dev)
+    kernels = finest_launch_ms(F, _lib, x0, bank, mode, max(3, args.steps), barrier)
+    vals = max_over_ranks(list(kernels.values()), world, dev)
+    kernels = dict(zip(kernels, vals))
 
     # end to end through the public API with host buffers (pinned), every step
     e2e_steps = max(1, min(args.steps, 10))
     e2e_ms = float("nan")
     if args.no_e2e:
         return _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms,
-                            launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
-    xh = x0.cpu().pin_memory()
-    gh = torch.empty_like(xh).pin_memory()
-    xd = torch.empty_like(x0)
-    for _ in range(max(1, args.warmup // 2)):
-        xd.copy_(xh, non_blocking=True)
-        xe = xd.detach().requires_grad_()
-        step(xe)
-        gh.copy_(xe.grad, non_blocking=True)
-        xe.grad = None
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        xd.copy_(xh, non_blocking=True)
-        xe = xd.detach().requires_grad_()
-        step(xe)
-        gh.copy_(xe.grad, non_blocking=True)
-        xe.grad = None
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+                            kernels, launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
+    e2e_ms = e2e_pipelined(step, x0, e2e_steps, max(1, args.warmup // 2), barrier)
     (e2e_ms,) = max_over_ranks([e2e_ms], world, dev)
     return _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms,
-                        launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
+                        kernels, launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
 
 
-def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms, launches,
-                 clk, pool, x0, e2e_steps, e2e_ms, shape):
+def e2e_pipelined(step, x0, steps, warmup, barrier):
+    """Device time of `steps` end-to-end steps: every step copies its input from pinned host
+    memory (host->device), runs the step through the public API and copies the result (the
+    input gradient, as large as the input) back to pinned host memory.  The copies run on
+    their own streams, double-buffered, so that step i+1's upload and step i's download overlap
+    step i's kernels and each other (PCIe is full duplex); the timed region runs from the first
+    upload to the last download."""
+    import torch
+    dev = x0.device
+    xh = x0.cpu().pin_memory()
+    gh = [torch.empty_like(xh).pin_memory() for _ in range(2)]
+    xd = [torch.empty_like(x0) for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=False)
+
+    def run(n, timed):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        uploaded = [ev() for _ in range(n)]
+        consumed = [None, None]   # compute done with xd[b]
+        computed = [ev() for _ in range(n)]
+        downloaded = [None, None]  # gh[b] and the gradient of the step that used b are free
+        grads = [None, None]
+        if timed:
+            start.record(s_in)
+        for i in range(n):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                if consumed[b] is not None:
+                    s_in.wait_event(consumed[b])
+                xd[b].copy_(xh, non_blocking=True)
+                uploaded[i].record(s_in)
+            comp.wait_event(uploaded[i])
+            if downloaded[b] is not None:
+                comp.wait_event(downloaded[b])
+            xe = xd[b].detach().requires_grad_()
+            step(xe)
+            grads[b] = xe.grad
+            consumed[b] = ev()
+            consumed[b].record(comp)
+            computed[i].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(computed[i])
+                gh[b].copy_(grads[b], non_blocking=True)
+                downloaded[b] = ev()
+                downloaded[b].record(s_out)
+        if timed:
+            end.record(s_out)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) if timed else 0.0
+
+    run(warmup, False)
+    barrier()
+    torch.cuda.synchronize()
+    return run(steps, True)
+
+
+def finest_launch_ms(F, _lib, x0, bank, mode, reps, barrier):
+    """Device time of one launch of each dominant kernel: the finest level of the analysis
+    (one-level dwt of the whole batch: dwt_ana_stream_kernel) and of the synthesis (one-level
+    idwt: dwt_syn_stream_kernel), each the largest launch of its direction in the step.  Timed
+    with CUDA events around `reps` back-to-back calls (each call must be one launch)."""
+    import torch
+    x2 = x0.reshape(-1, x0.shape[-1])
+    a1, d1 = F.dwt(x2, bank, mode)
+    out = {}
+    for name, fn in (("dwt_ana_stream_kernel<float,16>", lambda: F.dwt(x2, bank, mode)),
+                     ("dwt_syn_stream_kernel<float,16,0>", lambda: F.idwt(a1, d1, bank, mode))):
+        for _ in range(2):
+            fn()
+        barrier()
+        torch.cuda.synchronize()
+        l0 = _lib.launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        if _lib.launch_count() - l0 != reps:
+            raise RuntimeError(f"{name}: a one-level call was not exactly one launch")
+        out[name] = e0.elapsed_time(e1) / reps
+    return out
+
+
+def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms, kernels,
+                 launches, clk, pool, x0, e2e_steps, e2e_ms, shape):
     if rank != 0:
         return None
     peak, peak_src = peaks()
     value = job_throughput(step_bytes, args.steps, world, ms, 1e9)
-    kernels = {
-        "dwt_analysis_kernel<float,16>": ana_ms,
-        "dwt_syn_tile_kernel<float,16,0>": syn_ms,
-    }
     dominant = max(kernels, key=kernels.get)
     kern_ms = kernels[dominant]
     achieved = dir_bytes_row * R / (kern_ms / 1e3) / 1e9
@@ -339,6 +402,11 @@ def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, sy
             "launch_ms": round(kern_ms, 4),
             "traffic": TRAFFIC_PER_LAUNCH.get(dominant),
             "kernels_ms_per_launch": {k: round(v, 4) for k, v in kernels.items()},
+            "launch": "the finest level of the step's analysis / synthesis: one launch over "
+                      "every row, x (or the level-1 coefficients) read once, the other side "
+                      "written once",
+            "calls_ms": {"wavedec (8 levels, one launch per level)": round(ana_ms, 4),
+                         "waverec (8 levels, one launch per level)": round(syn_ms, 4)},
         },
         "gpu_launches": int(launches),
         "e2e": None if args.no_e2e else {
@@ -347,6 +415,9 @@ def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, sy
             "h2d_bytes_per_step": x0.numel() * 4,
             "d2h_bytes_per_step": x0.numel() * 4,
             "ms_per_step": round(e2e_ms / e2e_steps, 3),
+            "copies": "input upload and gradient download of every step on their own streams, "
+                      "double-buffered: step i+1's upload and step i's download overlap step "
+                      "i's kernels",
         },
         "clocks": clk.summary(),
     }

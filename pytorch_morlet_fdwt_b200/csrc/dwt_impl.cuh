@@ -974,10 +974,69 @@ int launch(K kern, const P& p, int64_t rows, int cs, size_t smem, cudaStream_t s
 template <typename T, int LM, bool ANALYSIS>
 int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
         const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
-        cudaStream_t stream, size_t* ws_needed) {
+        cudaStream_t stream, size_t* ws_needed, bool allow_stream = true);
+
+// Analysis whose finest levels stream (dwt_stream.cuh): each of the leading levels that
+// ana_streams() accepts runs as its own one-level launch, the approximations handed over
+// through two alternating workspace regions; the remaining (short-row) levels run on the
+// cluster kernel after them.  FDWT_ERR_UNSUPPORTED when the finest level does not stream.
+template <typename T, int LM>
+int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv, void* dst_final,
+                   const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
+                   cudaStream_t stream, size_t* ws_needed) {
+  const int nl = static_cast<int>(lv.size());
+  int c = 0;
+  while (c < nl && ana_streams<T, LM>(lv[c])) ++c;
+  if (c == 0) return FDWT_ERR_UNSUPPORTED;
+  size_t region[2] = {0, 0};
+  for (int k = 0; k < c && k < nl - 1; ++k) {
+    const size_t b = (static_cast<size_t>(rows) * lv[k].a_len * sizeof(T) + 255) & ~size_t(255);
+    region[k & 1] = std::max(region[k & 1], b);
+  }
+  const std::vector<Level> rest(lv.begin() + c, lv.end());
+  size_t rest_ws = 0;
+  if (!rest.empty()) {
+    const int st = run<T, LM, true>(rows, nullptr, rest, nullptr, h0, h1, L, off, nullptr, 0,
+                                    stream, &rest_ws, false);
+    if (st != FDWT_OK) return st;
+  }
+  const size_t need = region[0] + region[1] + rest_ws;
+  if (ws_needed) {
+    *ws_needed = need;
+    return FDWT_OK;
+  }
+  if (rows == 0) return FDWT_OK;
+  if (need > 0 && (ws == nullptr || ws_bytes < need)) return FDWT_ERR_WORKSPACE;
+  unsigned char* base = static_cast<unsigned char*>(ws);
+  unsigned char* reg[2] = {base, base + region[0]};
+  const void* src = src0;
+  for (int k = 0; k < c; ++k) {
+    void* a_out = k == nl - 1 ? dst_final : static_cast<void*>(reg[k & 1]);
+    int st = run_ana_stream<T, LM>(rows, src, lv[k], a_out, h0, h1, L, off, stream);
+    if (st == FDWT_ERR_UNSUPPORTED)  // e.g. a misaligned input: this level on the cluster kernel
+      st = run<T, LM, true>(rows, src, std::vector<Level>(1, lv[k]), a_out, h0, h1, L, off,
+                            nullptr, 0, stream, nullptr, false);
+    if (st != FDWT_OK) return st;
+    src = a_out;
+  }
+  if (rest.empty()) return FDWT_OK;
+  return run<T, LM, true>(rows, src, rest, dst_final, h0, h1, L, off,
+                          rest_ws ? base + region[0] + region[1] : nullptr, rest_ws, stream,
+                          nullptr, false);
+}
+
+template <typename T, int LM, bool ANALYSIS>
+int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
+        const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
+        cudaStream_t stream, size_t* ws_needed, bool allow_stream) {
   using A = typename AccOf<T>::type;
   using C = Cfg<T, LM>;
   const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
+  if (ANALYSIS && allow_stream) {
+    const int sa = run_ana_stages<T, LM>(rows, src0, lv, dst_final, h0, h1, L, off, ws, ws_bytes,
+                                         stream, ws_needed);
+    if (sa != FDWT_ERR_UNSUPPORTED) return sa;
+  }
   if (!ANALYSIS) {
     // independent output tiles when their staging fits; the cluster kernel otherwise
     const int ts = run_syn_tiles<T, LM>(rows, src0, lv, dst_final, h0, h1, L, off, ws,

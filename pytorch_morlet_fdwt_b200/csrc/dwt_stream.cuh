@@ -371,5 +371,298 @@ int run_syn_stream(int64_t rows, const void* a, const Level& L0, void* y, const 
   }
 }
 
+// ------------------------------------------------------------------------------ analysis
+//
+// One-level analysis (a, d) = A(x) of rows whose length is a multiple of 16 bytes, every tile
+// of every row on the same persistent, bulk-copy-fed ring: tile t computes the outputs
+// [t T, t T + T) from the input positions [2 t T + off - (LM - 1), 2 t T + 2 T + off - 1] of the
+// extended signal.  The in-range part arrives by one cp.async.bulk; the few extended positions
+// outside [0, n) that the tile's outputs read (at most LM - 1 at each row end) are gathered by
+// the threads through the boundary map (ext_index) into the slot before its copy is issued.
+// An item is V = 48 bytes / 2 element sizes of consecutive outputs (6 in fp32, 3 in fp64), so
+// the windows of consecutive lanes start 48 bytes apart: their 128-bit loads hit distinct bank
+// groups in every quarter warp.
+
+template <typename A>
+constexpr int ana_stream_v() { return sizeof(A) == 8 ? 3 : 6; }
+template <typename A>
+constexpr int ana_stream_tile() { return 2 * SNT * ana_stream_v<A>(); }
+
+template <typename A, int LM>
+struct AnaStreamParams {
+  const A* x;        // (rows, n)
+  A* ap;             // (rows, a_len) approximation (a_len = nc or nc + 1: trailing zero)
+  A* dp;             // (rows, nc) details
+  int* err;          // device error word
+  int64_t ntile;     // rows * tiles
+  int64_t P;         // period of the boundary mode
+  int32_t n, nc, a_len, off, mode, tiles, span;
+  int32_t T;         // outputs per tile (a multiple of 2 V)
+  alignas(16) A taps[2 * LM];  // (h0[j], h1[j]) interleaved
+};
+
+// V outputs (a, d) from the window xw[R .. R + 2V + LM - 2) (xw 16-byte aligned): output v is
+// sum_j h[j] w[2v + LM - 1 - j], the recursion of ana_compute.
+template <typename A, int LM, int R>
+__device__ __forceinline__ void ana_stream_item(const AnaStreamParams<A, LM>& p, const A* xw,
+                                                A* ra, A* rd) {
+  constexpr int V = ana_stream_v<A>();
+  constexpr int W = 2 * V + LM - 2;
+  constexpr int VW = 16 / static_cast<int>(sizeof(A));
+  constexpr int NL = (R + W + VW - 1) / VW;
+  A w[NL * VW];
+#pragma unroll
+  for (int k = 0; k < NL; ++k) load16<A>(xw + k * VW, w + k * VW);
+  if constexpr (sizeof(A) == 4) {
+    unsigned long long acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = 0ull;
+#pragma unroll
+    for (int i = W - 1; i >= 0; --i) {
+      const unsigned long long xx = pair(w[R + i], w[R + i]);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const int j = 2 * v + LM - 1 - i;
+        if (j >= 0 && j < LM)
+          ffma2(acc[v], *reinterpret_cast<const unsigned long long*>(&p.taps[2 * j]), xx);
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      ra[v] = lo32(acc[v]);
+      rd[v] = hi32(acc[v]);
+    }
+  } else {
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      A a = A(0), d = A(0);
+#pragma unroll
+      for (int j = 0; j < LM; ++j) {
+        const A xv = w[R + 2 * v + LM - 1 - j];
+        a = fma(p.taps[2 * j], xv, a);
+        d = fma(p.taps[2 * j + 1], xv, d);
+      }
+      ra[v] = a;
+      rd[v] = d;
+    }
+  }
+}
+
+// Store the first `count` of V values at dst (8-byte stores of pairs when dst is 8-byte aligned).
+template <typename A, int V>
+__device__ __forceinline__ void store_run(A* dst, const A* v, int count) {
+  if constexpr (sizeof(A) == 4 && V % 2 == 0) {
+    if (count == V && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+#pragma unroll
+      for (int k = 0; k < V; k += 2) *reinterpret_cast<float2*>(dst + k) = make_float2(v[k], v[k + 1]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < V; ++k)
+    if (k < count) dst[k] = v[k];
+}
+
+template <typename A, int LM, int R>
+__device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint64_t* bar) {
+  constexpr int V = ana_stream_v<A>();
+  const int T = p.T;
+  const int tid = threadIdx.x;
+  const int64_t G = gridDim.x;
+  const int span = p.span, n = p.n;
+  const int pmin = p.off - (LM - 1);       // first extended position an output reads
+  const int pmax = 2 * (p.nc - 1) + p.off;  // last
+  auto slot = [&](int s) { return ring + static_cast<size_t>(s) * span; };
+  auto slot_lo = [&](int t) { return 2 * t * T + pmin - R; };  // a multiple of 16 bytes
+  // all threads: the extended positions outside [0, n) that tile g's outputs read, gathered
+  // through the boundary map with element-wise cp.async (one commit group per call, so that
+  // a thread's group count advances by one per tile)
+  auto ext_fill = [&](int64_t g, int s) {
+    const int64_t row = g / p.tiles;
+    const int xlo = slot_lo(static_cast<int>(g % p.tiles));
+    const A* xr = p.x + row * n;
+    A* sl = slot(s);
+    const int l1 = min(xlo + span, 0), r1 = min(xlo + span, pmax + 1);
+    auto one = [&](int q) {
+      const int64_t e = ext_index(q, n, p.mode, p.P);
+      if (e < 0) sl[q - xlo] = A(0);
+      else cp_async(sl + (q - xlo), xr + e, sizeof(A));
+    };
+    for (int q = max(xlo, pmin) + tid; q < l1; q += SNT) one(q);
+    for (int q = max(xlo, n) + tid; q < r1; q += SNT) one(q);
+    cp_async_commit();
+  };
+  // one thread: the bulk copy of tile g's in-range input into slot s
+  auto issue = [&](int64_t g, int s) {
+    const int64_t row = g / p.tiles;
+    const int xlo = slot_lo(static_cast<int>(g % p.tiles));
+    const int lo = max(xlo, 0), hi = min(xlo + span, n);
+    const unsigned bytes = static_cast<unsigned>(max(hi - lo, 0)) * sizeof(A);
+    mbar_expect_tx(&bar[s], bytes);
+    if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * n + lo, bytes, &bar[s]);
+  };
+  // the gathers of tile k form the k-th commit group of every thread; the group of tile k + 1
+  // is waited for before the barrier that ends tile k
+#pragma unroll 1
+  for (int s = 0; s < kStreamStages; ++s) {
+    const int64_t g = blockIdx.x + s * G;
+    if (g < p.ntile) ext_fill(g, s);
+    else cp_async_commit();
+  }
+  cp_async_wait<kStreamStages - 1>();
+  __syncthreads();
+  if (tid == 0) {
+#pragma unroll 1
+    for (int s = 0; s < kStreamStages; ++s) {
+      const int64_t g = blockIdx.x + s * G;
+      if (g < p.ntile) issue(g, s);
+    }
+  }
+  int k = 0;
+#pragma unroll 1
+  for (int64_t g = blockIdx.x; g < p.ntile; g += G, ++k) {
+    const int s = k % kStreamStages;
+    const unsigned par = static_cast<unsigned>(k / kStreamStages) & 1u;
+    const bool ok = mbar_wait_bounded(&bar[s], par);
+    if (ok) {
+      const int64_t row = g / p.tiles;
+      const int t = static_cast<int>(g % p.tiles);
+      A* arow = p.ap + row * p.a_len;
+      A* drow = p.dp + row * p.nc;
+      const A* sl = slot(s);
+#pragma unroll 1
+      for (int it = tid; it < T / V; it += SNT) {
+        const int o0 = t * T + V * it;
+        if (o0 >= p.nc) break;
+        A ra[V], rd[V];
+        ana_stream_item<A, LM, R>(p, sl + 2 * V * it, ra, rd);
+        const int cnt = min(V, p.nc - o0);
+        store_run<A, V>(drow + o0, rd, cnt);
+        store_run<A, V>(arow + o0, ra, cnt);
+      }
+      if (t == p.tiles - 1 && tid == 0)
+        for (int q = p.nc; q < p.a_len; ++q) arow[q] = A(0);  // transpose of waverec's trim
+    }
+    cp_async_wait<kStreamStages - 2>();  // this thread's gathers of tile k + 1
+    if (__syncthreads_or(!ok)) {
+      cp_async_wait<0>();
+      if (tid == 0) {
+        atomicExch(p.err, kErrCopyTimeout);
+#pragma unroll 1
+        for (int j = 0; j < kStreamStages; ++j) {
+          const int64_t gj = g + j * G;
+          if (gj >= p.ntile) break;
+          const int kj = k + j;
+          mbar_wait_bounded(&bar[kj % kStreamStages],
+                            static_cast<unsigned>(kj / kStreamStages) & 1u);
+        }
+      }
+      return;
+    }
+    const int64_t gn = g + kStreamStages * G;
+    if (gn < p.ntile) {
+      ext_fill(gn, s);
+      if (tid == 0) issue(gn, s);
+    } else {
+      cp_async_commit();
+    }
+  }
+}
+
+template <typename A, int LM>
+__global__ void __launch_bounds__(SNT, 3)
+dwt_ana_stream_kernel(const __grid_constant__ AnaStreamParams<A, LM> p, int r) {
+  extern __shared__ __align__(16) unsigned char ring_smem[];
+  __shared__ __align__(8) uint64_t bar[kStreamStages];
+  A* ring = reinterpret_cast<A*>(ring_smem);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStreamStages; ++s) mbar_init(&bar[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  if constexpr (sizeof(A) == 4) {
+    switch (r) {
+      case 0: ana_stream_tiles<A, LM, 0>(p, ring, bar); break;
+      case 1: ana_stream_tiles<A, LM, 1>(p, ring, bar); break;
+      case 2: ana_stream_tiles<A, LM, 2>(p, ring, bar); break;
+      default: ana_stream_tiles<A, LM, 3>(p, ring, bar); break;
+    }
+  } else {
+    if (r == 0) ana_stream_tiles<A, LM, 0>(p, ring, bar);
+    else ana_stream_tiles<A, LM, 1>(p, ring, bar);
+  }
+}
+
+// The analysis of level L0 as the streaming kernel when the shape allows it: element type with
+// fp32 / fp64 accumulation, LM <= kStreamMaxLM, rows of a multiple of 16 bytes and at least
+// kStreamMinOut samples.  Shape-only test (pointers are checked at launch).
+template <typename T, int LM>
+bool ana_streams(const Level& L0) {
+  using A = typename AccOf<T>::type;
+  constexpr int VW = 16 / static_cast<int>(sizeof(A));
+  return std::is_same<T, A>::value && LM <= kStreamMaxLM && L0.n_in >= kStreamMinOut &&
+         L0.n_in % VW == 0 && L0.n_in <= 0x3fffffffLL && L0.a_len <= L0.n_coef + 1;
+}
+
+// Runs the one-level analysis of L0 (x: rows x L0.n_in; approximation to a_out, rows x a_len;
+// details to L0.detail) on the streaming kernel; FDWT_ERR_UNSUPPORTED when it does not apply.
+template <typename T, int LM>
+int run_ana_stream(int64_t rows, const void* x, const Level& L0, void* a_out, const double* h0,
+                   const double* h1, int L, int off, cudaStream_t stream) {
+  using A = typename AccOf<T>::type;
+  if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
+    return FDWT_ERR_UNSUPPORTED;
+  } else {
+    constexpr int VW = 16 / static_cast<int>(sizeof(A));
+    constexpr int V = ana_stream_v<A>();
+    if (!ana_streams<T, LM>(L0) || x == nullptr || a_out == nullptr || L0.detail == nullptr ||
+        rows <= 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+      return FDWT_ERR_UNSUPPORTED;
+    const int64_t nc = L0.n_coef;
+    if (nc < 1) return FDWT_ERR_UNSUPPORTED;
+    // tiles of ana_stream_tile outputs; a short row is one tile rounded to 64 items
+    const int64_t T_s = std::min<int64_t>(ana_stream_tile<A>(), cdiv(nc, 64 * V) * 64 * V);
+    const int pmin = off - (LM - 1);
+    const int R = ((pmin % VW) + VW) % VW;
+    constexpr int W = 2 * V + LM - 2;
+    const int NL = (R + W + VW - 1) / VW;
+    const int span = static_cast<int>(2 * T_s - 2 * V + NL * VW);
+    const int64_t tiles = cdiv(nc, T_s);
+    if (rows * tiles > (1LL << 40)) return FDWT_ERR_UNSUPPORTED;
+    AnaStreamParams<A, LM> p{};
+    p.x = static_cast<const A*>(x);
+    p.ap = static_cast<A*>(a_out);
+    p.dp = static_cast<A*>(L0.detail);
+    p.err = device_error_flag();
+    if (p.err == nullptr) return FDWT_ERR_CUDA;
+    p.ntile = rows * tiles;
+    p.P = L0.P;
+    p.n = static_cast<int>(L0.n_in);
+    p.nc = static_cast<int>(nc);
+    p.a_len = static_cast<int>(L0.a_len);
+    p.off = off;
+    p.mode = L0.mode;
+    p.tiles = static_cast<int>(tiles);
+    p.span = span;
+    p.T = static_cast<int>(T_s);
+    for (int j = 0; j < LM; ++j) {
+      p.taps[2 * j] = j < L ? static_cast<A>(h0[j]) : A(0);
+      p.taps[2 * j + 1] = j < L ? static_cast<A>(h1[j]) : A(0);
+    }
+    const size_t smem = static_cast<size_t>(kStreamStages) * span * sizeof(A);
+    auto kern = dwt_ana_stream_kernel<A, LM>;
+    int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
+    if (st != FDWT_OK) return st;
+    int occ = 0;
+    FDWT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, SNT, smem));
+    if (occ < 1) return FDWT_ERR_UNSUPPORTED;
+    const int64_t grid = std::min<int64_t>(p.ntile, static_cast<int64_t>(occ) * sm_count());
+    if ((st = pre_launch(stream)) != FDWT_OK) return st;
+    kern<<<static_cast<unsigned>(grid), SNT, smem, stream>>>(p, R);
+    return launch_status();
+  }
+}
+
 }  // namespace dwtk
 }  // namespace fdwt

@@ -264,3 +264,36 @@ def test_one_level_synthesis_long_rows(wname, mode, nc, dtype, tol):
     close(F.waverec(coeffs, bank, mode), D.waverec(ref, tb, mode), tol)
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.float64, 1e-12)])
+@pytest.mark.parametrize("wname,mode,n", [("db8", "periodization", 65536), ("db8", "symmetric", 16384),
+                                          ("db4", "reflect", 12288), ("haar", "zero", 4096),
+                                          ("db10", "periodic", 8192), ("db12", "periodization", 6148),
+                                          ("db7", "symmetric", 4104), ("db20", "symmetric", 8192)])
+def test_one_level_analysis_long_rows(wname, mode, n, dtype, tol):
+    """One-level analyses of rows of a multiple of 16 bytes: every tile on the streaming kernel
+    (bulk copies through an mbarrier ring, the extended positions past the row ends gathered
+    through the boundary map; filters up to 24 taps -- db20 stays on the cluster kernel), as a
+    single level and as the finest levels of a deeper wavedec, forward and backward (the
+    backward of waverec is an analysis whose approximation carries a trailing zero)."""
+    torch.manual_seed(12)
+    bank = F.get_filter_bank(wname)
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    x = torch.randn(5, n, dtype=dtype, device=DEV)
+    a, d = F.dwt(x, bank, mode)
+    ra, rd = D.dwt(x.double().cpu().numpy(), tb, mode)
+    close(a, ra, tol)
+    close(d, rd, tol)
+    coeffs = F.wavedec(x, bank, mode, 4)
+    ref = D.wavedec(x.double().cpu().numpy(), tb, mode, 4)
+    for c, r in zip(coeffs, ref):
+        close(c, r, tol)
+    cg = [c.clone().requires_grad_() for c in coeffs]
+    y = F.waverec(cg, bank, mode)
+    gy = torch.randn_like(y)
+    (y * gy).sum().backward()
+    for c, r in zip(cg, D.waverec_vjp(ref, gy.double().cpu().numpy(), tb, mode)):
+        close(c.grad, r, tol)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
