@@ -767,6 +767,7 @@ constexpr int kLM[] = {2, 4, 6, 8, 10, 12, 16, 20, 24, 32, 40, 64};
 
 #include "dwt_syn_tile.cuh"
 #include "dwt_stream.cuh"
+#include "dwt_stream2.cuh"
 
 namespace fdwt {
 namespace dwtk {
@@ -976,22 +977,39 @@ int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
         const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
         cudaStream_t stream, size_t* ws_needed, bool allow_stream = true);
 
-// Analysis whose finest levels stream (dwt_stream.cuh): each of the leading levels that
-// ana_streams() accepts runs as its own one-level launch, the approximations handed over
-// through two alternating workspace regions; the remaining (short-row) levels run on the
-// cluster kernel after them.  FDWT_ERR_UNSUPPORTED when the finest level does not stream.
+// Analysis whose finest levels stream (dwt_stream.cuh, dwt_stream2.cuh): from the finest level
+// on, each pair of levels that fuses runs as one two-level pass, else each level that streams as
+// a one-level pass; the approximations are handed over through two alternating workspace
+// regions; the remaining (short-row) levels run on the cluster kernel after them.
+// FDWT_ERR_UNSUPPORTED when the finest level does not stream (or x is not 16-byte aligned).
 template <typename T, int LM>
 int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv, void* dst_final,
                    const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
                    cudaStream_t stream, size_t* ws_needed) {
   const int nl = static_cast<int>(lv.size());
+  if (ws_needed == nullptr && (reinterpret_cast<uintptr_t>(src0) & 15) != 0)
+    return FDWT_ERR_UNSUPPORTED;
+  std::vector<std::pair<int, int>> stages;  // (first level, levels)
   int c = 0;
-  while (c < nl && ana_streams<T, LM>(lv[c])) ++c;
-  if (c == 0) return FDWT_ERR_UNSUPPORTED;
+  while (c < nl) {
+    if (c + 1 < nl && plan_ana2<T, LM>(std::max<int64_t>(rows, 1), lv[c], lv[c + 1], off).ok) {
+      stages.emplace_back(c, 2);
+      c += 2;
+    } else if (ana_streams<T, LM>(lv[c])) {
+      stages.emplace_back(c, 1);
+      c += 1;
+    } else {
+      break;
+    }
+  }
+  if (stages.empty()) return FDWT_ERR_UNSUPPORTED;
+  const int ns = static_cast<int>(stages.size());
   size_t region[2] = {0, 0};
-  for (int k = 0; k < c && k < nl - 1; ++k) {
-    const size_t b = (static_cast<size_t>(rows) * lv[k].a_len * sizeof(T) + 255) & ~size_t(255);
-    region[k & 1] = std::max(region[k & 1], b);
+  for (int i = 0; i < ns; ++i) {
+    const int last = stages[i].first + stages[i].second - 1;
+    if (last == nl - 1) continue;
+    const size_t b = (static_cast<size_t>(rows) * lv[last].a_len * sizeof(T) + 255) & ~size_t(255);
+    region[i & 1] = std::max(region[i & 1], b);
   }
   const std::vector<Level> rest(lv.begin() + c, lv.end());
   size_t rest_ws = 0;
@@ -1010,10 +1028,13 @@ int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv,
   unsigned char* base = static_cast<unsigned char*>(ws);
   unsigned char* reg[2] = {base, base + region[0]};
   const void* src = src0;
-  for (int k = 0; k < c; ++k) {
-    void* a_out = k == nl - 1 ? dst_final : static_cast<void*>(reg[k & 1]);
-    int st = run_ana_stream<T, LM>(rows, src, lv[k], a_out, h0, h1, L, off, stream);
-    if (st == FDWT_ERR_UNSUPPORTED)  // e.g. a misaligned input: this level on the cluster kernel
+  for (int i = 0; i < ns; ++i) {
+    const int k = stages[i].first, m = stages[i].second;
+    void* a_out = k + m - 1 == nl - 1 ? dst_final : static_cast<void*>(reg[i & 1]);
+    int st = m == 2 ? run_ana2_stream<T, LM>(rows, src, lv[k], lv[k + 1], a_out, h0, h1, L, off,
+                                             stream)
+                    : run_ana_stream<T, LM>(rows, src, lv[k], a_out, h0, h1, L, off, stream);
+    if (st == FDWT_ERR_UNSUPPORTED && m == 1)  // this level on the cluster kernel
       st = run<T, LM, true>(rows, src, std::vector<Level>(1, lv[k]), a_out, h0, h1, L, off,
                             nullptr, 0, stream, nullptr, false);
     if (st != FDWT_OK) return st;

@@ -402,10 +402,9 @@ struct AnaStreamParams {
 };
 
 // V outputs (a, d) from the window xw[R .. R + 2V + LM - 2) (xw 16-byte aligned): output v is
-// sum_j h[j] w[2v + LM - 1 - j], the recursion of ana_compute.
+// sum_j h[j] w[2v + LM - 1 - j], the recursion of ana_compute; taps = (h0[j], h1[j]) pairs.
 template <typename A, int LM, int R>
-__device__ __forceinline__ void ana_stream_item(const AnaStreamParams<A, LM>& p, const A* xw,
-                                                A* ra, A* rd) {
+__device__ __forceinline__ void ana_window_item(const A* taps, const A* xw, A* ra, A* rd) {
   constexpr int V = ana_stream_v<A>();
   constexpr int W = 2 * V + LM - 2;
   constexpr int VW = 16 / static_cast<int>(sizeof(A));
@@ -424,7 +423,7 @@ __device__ __forceinline__ void ana_stream_item(const AnaStreamParams<A, LM>& p,
       for (int v = 0; v < V; ++v) {
         const int j = 2 * v + LM - 1 - i;
         if (j >= 0 && j < LM)
-          ffma2(acc[v], *reinterpret_cast<const unsigned long long*>(&p.taps[2 * j]), xx);
+          ffma2(acc[v], *reinterpret_cast<const unsigned long long*>(&taps[2 * j]), xx);
       }
     }
 #pragma unroll
@@ -439,8 +438,8 @@ __device__ __forceinline__ void ana_stream_item(const AnaStreamParams<A, LM>& p,
 #pragma unroll
       for (int j = 0; j < LM; ++j) {
         const A xv = w[R + 2 * v + LM - 1 - j];
-        a = fma(p.taps[2 * j], xv, a);
-        d = fma(p.taps[2 * j + 1], xv, d);
+        a = fma(taps[2 * j], xv, a);
+        d = fma(taps[2 * j + 1], xv, d);
       }
       ra[v] = a;
       rd[v] = d;
@@ -535,7 +534,7 @@ __device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint6
         const int o0 = t * T + V * it;
         if (o0 >= p.nc) break;
         A ra[V], rd[V];
-        ana_stream_item<A, LM, R>(p, sl + 2 * V * it, ra, rd);
+        ana_window_item<A, LM, R>(p.taps, sl + 2 * V * it, ra, rd);
         const int cnt = min(V, p.nc - o0);
         store_run<A, V>(drow + o0, rd, cnt);
         store_run<A, V>(arow + o0, ra, cnt);
