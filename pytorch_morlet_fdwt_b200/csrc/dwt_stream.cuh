@@ -99,10 +99,11 @@ __device__ __forceinline__ void load16(const A* s, A* r) {
 }
 
 // Outputs [p0, p0 + 8) from the windows aw[R .. R + NWIN), dw[R .. R + NWIN) (aw, dw 16-byte
-// aligned): the packed-tap recursion of tile_item on a dense window.
+// aligned): the packed-tap recursion of tile_item on a dense window; hp = the packed taps
+// (h0[m], h0[m-1]) for m = 0..LM followed by those of h1.
 template <typename A, int LM, int C0, int R>
-__device__ __forceinline__ void stream_item(const StreamParams<A, LM>& p, const A* aw,
-                                            const A* dw, A (&z)[2 * TQ]) {
+__device__ __forceinline__ void syn_window_item(const A* hp, const A* aw, const A* dw,
+                                                A (&z)[2 * TQ]) {
   constexpr int NV = LM / 2 + 1;
   constexpr int NWIN = TQ + NV - 1;
   constexpr int VW = 16 / static_cast<int>(sizeof(A));
@@ -127,8 +128,8 @@ __device__ __forceinline__ void stream_item(const StreamParams<A, LM>& p, const 
     const int m = 2 * v - C0;
     if (m < 0 || m > LM) continue;  // resolved at compile time
     Pair<A> ha, hd;
-    ha.load(&p.hp[2 * m]);
-    hd.load(&p.hp[2 * (LM + 1) + 2 * m]);
+    ha.load(&hp[2 * m]);
+    hd.load(&hp[2 * (LM + 1) + 2 * m]);
 #pragma unroll
     for (int q = 0; q < TQ; ++q) {
       acc[q].fma(ha, xa[q + v]);
@@ -210,7 +211,7 @@ __device__ void stream_tiles(const StreamParams<A, LM>& p, A* ring, uint64_t* ba
         const int p0 = ms + 8 * it;
         if (p0 >= p.n_out) break;
         A z[2 * TQ];
-        stream_item<A, LM, C0, R>(p, as + 4 * it, ds + 4 * it, z);
+        syn_window_item<A, LM, C0, R>(p.hp, as + 4 * it, ds + 4 * it, z);
         if (p0 + 8 <= p.n_out) {
           store_vec<A, 2 * TQ>(yrow + p0, z);
         } else {
@@ -300,8 +301,9 @@ int run_syn_stream(int64_t rows, const void* a, const Level& L0, void* y, const 
                                 : kFillNone;
     // filling stages take every tile (rows of one short tile included); the others leave the
     // tiles near the row ends to the tile kernel, whose tiles then must be the same
-    const int64_t T_s = fill != kFillNone ? std::min<int64_t>(T_full, (n_out + 63) / 64 * 64)
-                                          : T_full;
+    const int64_t T_s = fill != kFillNone  // tiles of equal size, at most T_full outputs
+                            ? cdiv(cdiv(n_out, cdiv(n_out, T_full)), 64) * 64
+                            : T_full;
     const int span = static_cast<int>(T_s / 2 - 4 + NL * VW);  // a multiple of VW
     const int64_t tiles = cdiv(n_out, T_s);
     auto slot_lo = [&](int64_t t) { return ((t * T_s - off - C0) >> 1) - R; };
@@ -620,8 +622,8 @@ int run_ana_stream(int64_t rows, const void* x, const Level& L0, void* a_out, co
       return FDWT_ERR_UNSUPPORTED;
     const int64_t nc = L0.n_coef;
     if (nc < 1) return FDWT_ERR_UNSUPPORTED;
-    // tiles of ana_stream_tile outputs; a short row is one tile rounded to 64 items
-    const int64_t T_s = std::min<int64_t>(ana_stream_tile<A>(), cdiv(nc, 64 * V) * 64 * V);
+    // tiles of equal size, at most ana_stream_tile outputs (a multiple of 2V)
+    const int64_t T_s = cdiv(cdiv(nc, cdiv(nc, ana_stream_tile<A>())), 2 * V) * 2 * V;
     const int pmin = off - (LM - 1);
     const int R = ((pmin % VW) + VW) % VW;
     constexpr int W = 2 * V + LM - 2;

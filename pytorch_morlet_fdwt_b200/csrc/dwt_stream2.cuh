@@ -244,8 +244,10 @@ Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int of
     const int NL = (R + W + VW - 1) / VW;
     const int kh = (-pmin + V - 1) / V;
     const int kr = (std::max(off - 1, 0) + V - 1) / V;
-    // one level-k item per thread: K1 = kh + T1 / V + kr <= SNT
-    const int T2 = V * ((SNT - kh - kr) / 2);
+    // one level-k item per thread: K1 = kh + T1 / V + kr <= SNT; then tiles of equal size
+    const int q_max = (SNT - kh - kr) / 2;
+    const int64_t n_tiles = cdiv(nc2, static_cast<int64_t>(V) * q_max);
+    const int T2 = V * static_cast<int>(cdiv(cdiv(nc2, n_tiles), V));
     const int T1 = 2 * T2;
     const int K1 = kh + T1 / V + kr;
     const int span = 2 * V * K1 - 2 * V + NL * VW;
@@ -323,6 +325,331 @@ int run_ana2_stream(int64_t rows, const void* x, const Level& L1, const Level& L
       p.taps[2 * j + 1] = j < L ? static_cast<A>(h1[j]) : A(0);
     }
     auto kern = dwt_ana2_stream_kernel<A, LM>;
+    int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
+    if (st != FDWT_OK) return st;
+    int occ = 0;
+    FDWT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, SNT, pl.smem));
+    if (occ < 1) return FDWT_ERR_UNSUPPORTED;
+    const int64_t grid = std::min<int64_t>(p.ntile, static_cast<int64_t>(occ) * sm_count());
+    if ((st = pre_launch(stream)) != FDWT_OK) return st;
+    kern<<<static_cast<unsigned>(grid), SNT, pl.smem, stream>>>(p, pl.R);
+    return launch_status();
+  }
+}
+
+// ------------------------------------------------------------------------------ synthesis
+//
+// Levels k+1 and k of a multilevel synthesis in one pass (periodization or zero mode, the two
+// that stream every tile): a tile owns T outputs of y (level k).  Their windows read the
+// level-k approximation a1 and the details d1 over one slot range [glo, glo + span), exactly
+// as the one-level kernel.  a1 there is computed from a slot of a2 and d2 into a shared buffer
+// (items of 8 a1 values; the buffer range is recomputed by both tiles that overlap in it), d1
+// arrives by bulk copy with the slot, and after a barrier the y items run.  a1 never touches
+// HBM.  In zero mode the buffer cells outside [0, nc1) are set to 0 (the coefficients that
+// level k reads there are zero); in periodization the values computed from the periodically
+// continued a2, d2 are already a1's continuation.  The a1 items start delta - 8 cells before
+// glo (delta even, < 2 VW, one per launch), which gives their a2/d2 windows the same 16-byte
+// shift R as the y windows.
+
+template <typename A, int LM>
+struct Syn2Params {
+  const A* a2;       // (rows, a2_stride) level-(k+1) approximation
+  const A* d2;       // (rows, nc2)
+  const A* d1;       // (rows, nc1)
+  A* y;              // (rows, n_out)
+  int* err;          // device error word
+  int64_t a2_stride;
+  int64_t ntile;     // rows * tiles
+  int32_t nc2, nc1, n_out, off, fill, tiles, T;
+  int32_t span;      // d1 (and buffer) cells per tile
+  int32_t span2;     // a2 / d2 cells per tile
+  int32_t M1, delta; // a1 items per tile and their start (see above)
+  int32_t abuf;      // buffer elements
+  alignas(16) A hp[2 * (LM + 1) * 2];
+};
+
+template <typename A, int LM, int C0, int R>
+__device__ void syn2_tiles(const Syn2Params<A, LM>& p, A* ring, A* abuf, uint64_t* bar) {
+  const int T = p.T;
+  const int tid = threadIdx.x;
+  const int64_t G = gridDim.x;
+  const int span = p.span, span2 = p.span2;
+  const int slot_elems = span + 2 * span2;
+  auto slot = [&](int s) { return ring + static_cast<size_t>(s) * slot_elems; };
+  auto glo_of = [&](int t) { return ((t * T - p.off - C0) >> 1) - R; };
+  auto g2lo_of = [&](int t) { return ((glo_of(t) - p.off - C0 + p.delta - 8) >> 1) - R; };
+  // zero mode: slot cells outside [0, nc) of the arrays of tile g (all threads)
+  auto zero_fill = [&](int64_t g, int s) {
+    if (p.fill != kFillZero) return;
+    const int t = static_cast<int>(g % p.tiles);
+    const int gl = glo_of(t), g2 = g2lo_of(t);
+    A* d1s = slot(s);
+    A* a2s = d1s + span;
+    A* d2s = a2s + span2;
+    for (int i = tid; i < -gl && i < span; i += SNT) d1s[i] = A(0);
+    for (int i = max(p.nc1 - gl, 0) + tid; i < span; i += SNT) d1s[i] = A(0);
+    for (int i = tid; i < -g2 && i < span2; i += SNT) a2s[i] = d2s[i] = A(0);
+    for (int i = max(p.nc2 - g2, 0) + tid; i < span2; i += SNT) a2s[i] = d2s[i] = A(0);
+  };
+  // one array's cells [lo_el, lo_el + cnt) of a row of length nc into dst: the in-range part by
+  // bulk copy, and in periodic mode the continuation past either end from the other end
+  auto copy_range = [&](A* dst, const A* row, int lo_el, int cnt, int nc, int s) {
+    const int lo = max(lo_el, 0), hi = min(lo_el + cnt, nc);
+    unsigned tx = 0;
+    if (hi > lo) {
+      bulk_g2s(dst + (lo - lo_el), row + lo, (hi - lo) * sizeof(A), &bar[s]);
+      tx += (hi - lo) * sizeof(A);
+    }
+    if (p.fill == kFillPeriodic) {
+      const int pre = max(0, -lo_el), suf = max(0, lo_el + cnt - nc);
+      if (pre) {
+        bulk_g2s(dst, row + (nc - pre), pre * sizeof(A), &bar[s]);
+        tx += pre * sizeof(A);
+      }
+      if (suf) {
+        bulk_g2s(dst + (nc - lo_el), row, suf * sizeof(A), &bar[s]);
+        tx += suf * sizeof(A);
+      }
+    }
+    return tx;
+  };
+  auto tx_range = [&](int lo_el, int cnt, int nc) {
+    const int lo = max(lo_el, 0), hi = min(lo_el + cnt, nc);
+    unsigned tx = hi > lo ? (hi - lo) * sizeof(A) : 0;
+    if (p.fill == kFillPeriodic)
+      tx += (max(0, -lo_el) + max(0, lo_el + cnt - nc)) * sizeof(A);
+    return tx;
+  };
+  auto issue = [&](int64_t g, int s) {
+    const int64_t row = g / p.tiles;
+    const int t = static_cast<int>(g % p.tiles);
+    const int gl = glo_of(t), g2 = g2lo_of(t);
+    mbar_expect_tx(&bar[s], tx_range(gl, span, p.nc1) + 2 * tx_range(g2, span2, p.nc2));
+    A* d1s = slot(s);
+    copy_range(d1s, p.d1 + row * p.nc1, gl, span, p.nc1, s);
+    copy_range(d1s + span, p.a2 + row * p.a2_stride, g2, span2, p.nc2, s);
+    copy_range(d1s + span + span2, p.d2 + row * p.nc2, g2, span2, p.nc2, s);
+  };
+#pragma unroll 1
+  for (int s = 0; s < kStreamStages; ++s) {
+    const int64_t g = blockIdx.x + s * G;
+    if (g < p.ntile) zero_fill(g, s);
+  }
+  __syncthreads();
+  if (tid == 0) {
+#pragma unroll 1
+    for (int s = 0; s < kStreamStages; ++s) {
+      const int64_t g = blockIdx.x + s * G;
+      if (g < p.ntile) issue(g, s);
+    }
+  }
+  int k = 0;
+#pragma unroll 1
+  for (int64_t g = blockIdx.x; g < p.ntile; g += G, ++k) {
+    const int s = k % kStreamStages;
+    const unsigned par = static_cast<unsigned>(k / kStreamStages) & 1u;
+    const bool ok = mbar_wait_bounded(&bar[s], par);
+    const int64_t row = g / p.tiles;
+    const int t = static_cast<int>(g % p.tiles);
+    const int gl = glo_of(t);
+    const A* d1s = slot(s);
+    const A* a2s = d1s + span;
+    const A* d2s = a2s + span2;
+    if (ok) {  // level k+1: a1 over the slot range (buffer cell q - glo + 8)
+#pragma unroll 1
+      for (int m = tid; m < p.M1; m += SNT) {
+        A z[2 * TQ];
+        syn_window_item<A, LM, C0, R>(p.hp, a2s + 4 * m, d2s + 4 * m, z);
+        A* b = abuf + p.delta + 8 * m;
+#pragma unroll
+        for (int q = 0; q < 2 * TQ; ++q) b[q] = z[q];
+      }
+    }
+    __syncthreads();
+    const int c_lo = p.delta, c_hi = p.delta + 8 * p.M1;  // computed buffer cells
+    if (p.fill == kFillZero && (gl + c_lo - 8 < 0 || gl + c_hi - 8 > p.nc1)) {
+      if (ok) {
+        for (int i = c_lo + tid; i < min(c_hi, 8 - gl); i += SNT) abuf[i] = A(0);
+        for (int i = max(c_lo, p.nc1 - gl + 8) + tid; i < c_hi; i += SNT) abuf[i] = A(0);
+      }
+      __syncthreads();
+    }
+    if (ok) {  // level k: y
+      A* yrow = p.y + row * p.n_out;
+      const int ms = t * T;
+#pragma unroll 1
+      for (int it = tid; it < T / 8; it += SNT) {
+        const int p0 = ms + 8 * it;
+        if (p0 >= p.n_out) break;
+        A z[2 * TQ];
+        syn_window_item<A, LM, C0, R>(p.hp, abuf + 8 + 4 * it, d1s + 4 * it, z);
+        if (p0 + 8 <= p.n_out) {
+          store_vec<A, 2 * TQ>(yrow + p0, z);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 2 * TQ; ++q)
+            if (p0 + q < p.n_out) yrow[p0 + q] = z[q];
+        }
+      }
+    }
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        atomicExch(p.err, kErrCopyTimeout);
+#pragma unroll 1
+        for (int j = 0; j < kStreamStages; ++j) {
+          const int64_t gj = g + j * G;
+          if (gj >= p.ntile) break;
+          const int kj = k + j;
+          mbar_wait_bounded(&bar[kj % kStreamStages],
+                            static_cast<unsigned>(kj / kStreamStages) & 1u);
+        }
+      }
+      return;
+    }
+    const int64_t gn = g + kStreamStages * G;
+    if (gn < p.ntile) {
+      zero_fill(gn, s);
+      if (tid == 0) issue(gn, s);
+    }
+  }
+}
+
+template <typename A, int LM, int C0>
+__global__ void __launch_bounds__(SNT, 2)
+dwt_syn2_stream_kernel(const __grid_constant__ Syn2Params<A, LM> p, int r) {
+  extern __shared__ __align__(16) unsigned char ring_smem[];
+  __shared__ __align__(8) uint64_t bar[kStreamStages];
+  A* ring = reinterpret_cast<A*>(ring_smem);
+  A* abuf = ring + static_cast<size_t>(kStreamStages) * (p.span + 2 * p.span2);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStreamStages; ++s) mbar_init(&bar[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  if constexpr (sizeof(A) == 4) {
+    switch (r) {
+      case 0: syn2_tiles<A, LM, C0, 0>(p, ring, abuf, bar); break;
+      case 1: syn2_tiles<A, LM, C0, 1>(p, ring, abuf, bar); break;
+      case 2: syn2_tiles<A, LM, C0, 2>(p, ring, abuf, bar); break;
+      default: syn2_tiles<A, LM, C0, 3>(p, ring, abuf, bar); break;
+    }
+  } else {
+    if (r == 0) syn2_tiles<A, LM, C0, 0>(p, ring, abuf, bar);
+    else syn2_tiles<A, LM, C0, 1>(p, ring, abuf, bar);
+  }
+}
+
+// Geometry of a fused synthesis pair: Lc (level k+1, processing order) then Lf (level k).
+template <typename T, int LM>
+struct Syn2Plan {
+  bool ok = false;
+  int R = 0;
+  Syn2Params<typename AccOf<T>::type, LM> p{};
+  size_t smem = 0;
+};
+
+template <typename T, int LM>
+Syn2Plan<T, LM> plan_syn2(int64_t rows, const Level& Lc, const Level& Lf, int off) {
+  using A = typename AccOf<T>::type;
+  Syn2Plan<T, LM> pl;
+  if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
+    return pl;
+  } else {
+    constexpr int VW = 16 / static_cast<int>(sizeof(A));
+    const int64_t nc2 = Lc.n_coef, a2_stride = Lc.a_len, n1 = Lc.n_in;
+    const int64_t nc1 = Lf.n_coef, n_out = Lf.n_in;
+    if (!stream_fills(Lc) || !stream_fills(Lf) || Lc.mode != Lf.mode || rows <= 0) return pl;
+    if (Lf.a_len != n1 || nc1 > n1 || n_out < kStreamMinOut || n_out > 0x3fffffffLL) return pl;
+    if (nc2 % VW || a2_stride % VW || nc1 % VW || n_out % VW) return pl;
+    if (Lc.mode == FDWT_MODE_PERIODIZATION && nc1 != n1) return pl;
+    const int fill = Lf.mode == FDWT_MODE_ZERO ? kFillZero : kFillPeriodic;
+    const int C0 = off & 1;
+    const int half = (off + C0) / 2;
+    const int R = ((-half) % VW + VW) % VW;
+    constexpr int NWIN = TQ + LM / 2;
+    const int NL = (R + NWIN + VW - 1) / VW;
+    const int Mmax = sizeof(A) == 8 ? SNT / 2 : SNT;  // a1 items per tile
+    // the largest tile whose a1 items fit one per thread, then tiles of equal size
+    const int T_max = 16 * VW * ((2 * (8 * Mmax - 4 - NL * VW)) / (16 * VW));
+    const int64_t n_tiles = cdiv(n_out, T_max);
+    const int Tt = static_cast<int>(cdiv(cdiv(n_out, n_tiles), 16 * VW) * 16 * VW);
+    const int span = Tt / 2 - 4 + NL * VW;
+    auto glo = [&](int64_t t) { return ((t * Tt - off - C0) >> 1) - R; };
+    const int64_t c0 = glo(0) - off - C0;
+    const int delta = static_cast<int>(((2 * R - c0) % (2 * VW) + 2 * VW) % (2 * VW));
+    const int M1 = (span + 8 - delta + 7) / 8;
+    const int span2 = 4 * (M1 - 1) + NL * VW;
+    int abuf = std::max(8 + span, delta + 8 * M1);
+    abuf = (abuf + VW - 1) / VW * VW;
+    const int64_t tiles = cdiv(n_out, Tt);
+    if (fill == kFillPeriodic) {  // one period at most on either side
+      auto g2lo = [&](int64_t t) { return ((glo(t) - off - C0 + delta - 8) >> 1) - R; };
+      if (-glo(0) > nc1 || glo(tiles - 1) + span - nc1 > nc1 || -g2lo(0) > nc2 ||
+          g2lo(tiles - 1) + span2 - nc2 > nc2)
+        return pl;
+    }
+    if (rows * tiles > (1LL << 40)) return pl;
+    auto& p = pl.p;
+    p.a2_stride = a2_stride;
+    p.ntile = rows * tiles;
+    p.nc2 = static_cast<int>(nc2);
+    p.nc1 = static_cast<int>(nc1);
+    p.n_out = static_cast<int>(n_out);
+    p.off = off;
+    p.fill = fill;
+    p.tiles = static_cast<int>(tiles);
+    p.T = Tt;
+    p.span = span;
+    p.span2 = span2;
+    p.M1 = M1;
+    p.delta = delta;
+    p.abuf = abuf;
+    pl.R = R;
+    pl.smem = (static_cast<size_t>(kStreamStages) * (span + 2 * span2) + abuf) * sizeof(A);
+    pl.ok = pl.smem <= static_cast<size_t>(max_smem_optin()) - 2048;
+    return pl;
+  }
+}
+
+template <typename T, int LM>
+bool syn2_fuses(int64_t rows, const Level& Lc, const Level& Lf, int off) {
+  return plan_syn2<T, LM>(rows, Lc, Lf, off).ok;
+}
+
+// Runs the synthesis levels Lc (coarser) and Lf (finer) in one streaming pass: a2 (rows x
+// Lc.a_len), Lc.detail and Lf.detail -> y (rows x Lf.n_in).  FDWT_ERR_UNSUPPORTED when the pair
+// does not fuse.
+template <typename T, int LM>
+int run_syn2_stream(int64_t rows, const void* a2, const Level& Lc, const Level& Lf, void* y,
+                    const double* h0, const double* h1, int L, int off, cudaStream_t stream) {
+  using A = typename AccOf<T>::type;
+  if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
+    return FDWT_ERR_UNSUPPORTED;
+  } else {
+    Syn2Plan<T, LM> pl = plan_syn2<T, LM>(rows, Lc, Lf, off);
+    auto aligned = [](const void* q) { return q && (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    if (!pl.ok || !aligned(a2) || !aligned(Lc.detail) || !aligned(Lf.detail) || !aligned(y))
+      return FDWT_ERR_UNSUPPORTED;
+    auto& p = pl.p;
+    p.a2 = static_cast<const A*>(a2);
+    p.d2 = static_cast<const A*>(Lc.detail);
+    p.d1 = static_cast<const A*>(Lf.detail);
+    p.y = static_cast<A*>(y);
+    p.err = device_error_flag();
+    if (p.err == nullptr) return FDWT_ERR_CUDA;
+    A hh0[LM], hh1[LM];
+    for (int j = 0; j < LM; ++j) {
+      hh0[j] = j < L ? static_cast<A>(h0[j]) : A(0);
+      hh1[j] = j < L ? static_cast<A>(h1[j]) : A(0);
+    }
+    for (int m = 0; m <= LM; ++m) {
+      p.hp[2 * m] = m < LM ? hh0[m] : A(0);
+      p.hp[2 * m + 1] = m >= 1 ? hh0[m - 1] : A(0);
+      p.hp[2 * (LM + 1) + 2 * m] = m < LM ? hh1[m] : A(0);
+      p.hp[2 * (LM + 1) + 2 * m + 1] = m >= 1 ? hh1[m - 1] : A(0);
+    }
+    auto kern = (off & 1) ? dwt_syn2_stream_kernel<A, LM, 1> : dwt_syn2_stream_kernel<A, LM, 0>;
     int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
     if (st != FDWT_OK) return st;
     int occ = 0;

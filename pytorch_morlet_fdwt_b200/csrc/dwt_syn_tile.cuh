@@ -718,17 +718,29 @@ int run_syn_stage(int64_t rows, const void* a, const std::vector<Level>& lv, voi
 }
 
 template <typename T, int LM>
+int run_syn2_stream(int64_t rows, const void* a2, const Level& Lc, const Level& Lf, void* y,
+                    const double* h0, const double* h1, int L, int off, cudaStream_t stream);
+template <typename T, int LM>
+bool syn2_fuses(int64_t rows, const Level& Lc, const Level& Lf, int off);
+
+template <typename T, int LM>
 int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, void* y,
                   const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
                   cudaStream_t stream, size_t* ws_needed) {
   using A = typename AccOf<T>::type;
   const int J = static_cast<int>(lv.size());
   const int64_t T_tile = tile_outputs<A>();
-  // stages, coarsest first: levels [0, cut[0]) together, then kSplitLevels levels per stage;
-  // stage s (but the last) hands its approximation to stage s + 1 through the workspace
-  std::vector<int> cut;  // first level of each fine stage
+  // stages in processing order: the coarse levels [0, c) together (if any), then the finer
+  // levels one or two per stage; each stage but the last hands its approximation to the next
+  // through the workspace
+  std::vector<std::pair<int, int>> fine;  // (first level, levels), finest first
   int c = J;
-  while (std::is_same<T, A>::value && c > kSplitLevels) {
+  while (std::is_same<T, A>::value && c > 0) {
+    if (c >= 2 && syn2_fuses<T, LM>(std::max<int64_t>(rows, 1), lv[c - 2], lv[c - 1], off)) {
+      fine.emplace_back(c - 2, 2);  // two levels per streaming pass (dwt_stream2.cuh)
+      c -= 2;
+      continue;
+    }
     // a level that streams every tile (dwt_stream.cuh) runs alone down to short rows; the
     // others while their rows are long
     const Level& f = lv[c - 1];
@@ -736,10 +748,15 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
     const bool streams = stream_fills(f) && LM <= kStreamMaxLM && f.n_in >= kStreamMinOut &&
                          f.n_in % VW == 0 && f.n_coef % VW == 0 && f.a_len % VW == 0;
     const bool alone = streams || (c > kSplitLevels + 1 && f.n_in >= 2 * T_tile);
-    if (!alone) break;
-    c -= kSplitLevels;
+    if (!alone || c == 1) break;
+    fine.emplace_back(c - 1, 1);
+    c -= 1;
   }
-  if (c == J) {
+  std::vector<std::pair<int, int>> stages;
+  if (c > 0) stages.emplace_back(0, c);
+  for (auto it = fine.rbegin(); it != fine.rend(); ++it) stages.push_back(*it);
+  const int ns = static_cast<int>(stages.size());
+  if (ns == 1) {
     if (ws_needed == nullptr && rows > 0)
       return run_syn_stage<T, LM>(rows, a, lv, y, h0, h1, L, off, stream);
     const int st = run_syn_tile_launch<T, LM>(rows, a, lv, y, h0, h1, L, off, stream,
@@ -747,18 +764,16 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
     if (st == FDWT_OK && ws_needed) *ws_needed = 0;
     return st;
   }
-  for (int k = c; k < J; k += kSplitLevels) cut.push_back(k);
-  const int ns = static_cast<int>(cut.size()) + 1;
   auto stage = [&](int s) {
-    const int b = s == 0 ? 0 : cut[s - 1];
-    const int e = s + 1 < ns ? cut[s] : J;
-    return std::vector<Level>(lv.begin() + b, lv.begin() + e);
+    return std::vector<Level>(lv.begin() + stages[s].first,
+                              lv.begin() + stages[s].first + stages[s].second);
   };
-  // the approximation stage s hands over has lv[cut[s]].a_len = lv[cut[s] - 1].n_in samples
-  // per row; the stage outputs alternate between two regions, the last-but-one in region 0
+  // stage s (but the last) outputs the n_in samples per row of its finest level; the outputs
+  // alternate between two regions, the last-but-one in region 0
   size_t region[2] = {0, 0};
   for (int s = 0; s + 1 < ns; ++s) {
-    const size_t bytes = (static_cast<size_t>(rows) * lv[cut[s] - 1].n_in * sizeof(T) + 255) &
+    const int last = stages[s].first + stages[s].second - 1;
+    const size_t bytes = (static_cast<size_t>(rows) * lv[last].n_in * sizeof(T) + 255) &
                          ~size_t(255);
     size_t& r = region[(ns - 2 - s) & 1];
     r = std::max(r, bytes);
@@ -779,7 +794,12 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
   const void* src = a;
   for (int s = 0; s < ns; ++s) {
     void* dst = s + 1 < ns ? static_cast<void*>(base[(ns - 2 - s) & 1]) : y;
-    const int st = run_syn_stage<T, LM>(rows, src, stage(s), dst, h0, h1, L, off, stream);
+    const auto lvs = stage(s);
+    int st = FDWT_ERR_UNSUPPORTED;
+    const bool pair = stages[s].second == 2 && (s > 0 || c == 0);  // a fused pair, not the coarse part
+    if (pair) st = run_syn2_stream<T, LM>(rows, src, lvs[0], lvs[1], dst, h0, h1, L, off, stream);
+    if (st == FDWT_ERR_UNSUPPORTED)
+      st = run_syn_stage<T, LM>(rows, src, lvs, dst, h0, h1, L, off, stream);
     if (st != FDWT_OK) return st;
     src = dst;
   }
