@@ -6,7 +6,8 @@
 Default workload (configs[1] of the baseline, the one the headline metric is quoted on):
 db8 ``periodization`` level-8 ``wavedec`` of x float32 (16, 128, 65536) i.i.d. N(0,1), ``waverec``
 of the coefficients, and the autograd backward through both.  One step = those four
-multilevel transforms over the whole batch (each a chain of one-level streaming launches);
+multilevel transforms over the whole batch (each a chain of streaming launches, two levels
+per launch where the shapes allow);
 inputs (512 MiB per array) are larger than the 126 MB L2.
 
 ``value`` is the whole-job algorithmic HBM throughput in GB/s (unique bytes the four transforms
@@ -39,12 +40,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "DWT/CWT achieved HBM GB/s (% of B200 peak); Morlet mixer tokens/s fwd+bwd"
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) per full-size launch of the finest-level kernels, from one ncu
-# capture of each on 1024 of the 2048 rows scaled by 2 (traffic grows with the rows); the
-# captures are summarised in profiles/dwt_cfg2_kernels.txt
+# DRAM bytes (read + write) per full-size launch of the kernels of the two finest levels, from
+# one ncu capture of each on 1024 of the 2048 rows scaled by 2 (traffic grows with the rows);
+# the captures are summarised in profiles/dwt_cfg2_kernels.txt
 TRAFFIC_PER_LAUNCH = {
-    "dwt_ana_stream_kernel<float,16>": 975_800_000,
-    "dwt_syn_stream_kernel<float,16,0>": 970_200_000,
+    "dwt_ana2_stream_kernel<float,16>": None,
+    "dwt_syn2_stream_kernel<float,16,0>": None,
 }
 
 
@@ -338,16 +339,17 @@ def e2e_pipelined(step, x0, steps, warmup, barrier):
 
 
 def finest_launch_ms(F, _lib, x0, bank, mode, reps, barrier):
-    """Device time of one launch of each dominant kernel: the finest level of the analysis
-    (one-level dwt of the whole batch: dwt_ana_stream_kernel) and of the synthesis (one-level
-    idwt: dwt_syn_stream_kernel), each the largest launch of its direction in the step.  Timed
-    with CUDA events around `reps` back-to-back calls (each call must be one launch)."""
+    """Device time of one launch of each dominant kernel: the two finest levels of the analysis
+    (a two-level wavedec of the whole batch: one dwt_ana2_stream_kernel launch) and of the
+    synthesis (a two-level waverec: one dwt_syn2_stream_kernel launch), each the largest launch
+    of its direction in the step.  Timed with CUDA events around `reps` back-to-back calls
+    (each call must be one launch)."""
     import torch
     x2 = x0.reshape(-1, x0.shape[-1])
-    a1, d1 = F.dwt(x2, bank, mode)
+    c2 = F.wavedec(x2, bank, mode, 2)
     out = {}
-    for name, fn in (("dwt_ana_stream_kernel<float,16>", lambda: F.dwt(x2, bank, mode)),
-                     ("dwt_syn_stream_kernel<float,16,0>", lambda: F.idwt(a1, d1, bank, mode))):
+    for name, fn in (("dwt_ana2_stream_kernel<float,16>", lambda: F.wavedec(x2, bank, mode, 2)),
+                     ("dwt_syn2_stream_kernel<float,16,0>", lambda: F.waverec(c2, bank, mode))):
         for _ in range(2):
             fn()
         barrier()
@@ -360,7 +362,7 @@ def finest_launch_ms(F, _lib, x0, bank, mode, reps, barrier):
         e1.record()
         torch.cuda.synchronize()
         if _lib.launch_count() - l0 != reps:
-            raise RuntimeError(f"{name}: a one-level call was not exactly one launch")
+            raise RuntimeError(f"{name}: a two-level call was not exactly one launch")
         out[name] = e0.elapsed_time(e1) / reps
     return out
 
@@ -402,11 +404,11 @@ def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, sy
             "launch_ms": round(kern_ms, 4),
             "traffic": TRAFFIC_PER_LAUNCH.get(dominant),
             "kernels_ms_per_launch": {k: round(v, 4) for k, v in kernels.items()},
-            "launch": "the finest level of the step's analysis / synthesis: one launch over "
-                      "every row, x (or the level-1 coefficients) read once, the other side "
-                      "written once",
-            "calls_ms": {"wavedec (8 levels, one launch per level)": round(ana_ms, 4),
-                         "waverec (8 levels, one launch per level)": round(syn_ms, 4)},
+            "launch": "the two finest levels of the step's analysis / synthesis in one launch "
+                      "over every row: x (or the level-1 details and level-2 coefficients) "
+                      "read once, the other side written once",
+            "calls_ms": {"wavedec (8 levels, 4 launches)": round(ana_ms, 4),
+                         "waverec (8 levels, 4 launches)": round(syn_ms, 4)},
         },
         "gpu_launches": int(launches),
         "e2e": None if args.no_e2e else {

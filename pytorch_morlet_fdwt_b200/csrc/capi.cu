@@ -1,5 +1,7 @@
 // Library-wide C ABI helpers: status strings, per-thread CUDA error, device attributes.
 #include <atomic>
+#include <map>
+#include <tuple>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -38,6 +40,28 @@ int sm_count() {
     cache[dev] = v;
   }
   return cache[dev];
+}
+
+int occupancy(const void* kernel, int threads, size_t smem, int* blocks) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t, int>, int> cache;
+  int dev = 0;
+  FDWT_CUDA(cudaGetDevice(&dev));
+  const auto key = std::make_tuple(kernel, threads, smem, dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) {
+      *blocks = it->second;
+      return FDWT_OK;
+    }
+  }
+  int v = 0;
+  FDWT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, threads, smem));
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = v;
+  *blocks = v;
+  return FDWT_OK;
 }
 
 int allow_max_dynamic_smem(const void* kernel) {

@@ -46,6 +46,9 @@ int sm_count();
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize = device opt-in limit), cached per
 // (kernel, device).
 int allow_max_dynamic_smem(const void* kernel);
+// Resident blocks per SM of `kernel` at `threads` threads and `smem` dynamic shared bytes on
+// the current device (cudaOccupancyMaxActiveBlocksPerMultiprocessor, cached per key).
+int occupancy(const void* kernel, int threads, size_t smem, int* blocks);
 // Called before every kernel launch: runs the shared-memory fill kernel of the test hook
 // fdwt_set_shared_memory_fill when it is enabled (FDWT_OK and nothing otherwise).
 int pre_launch(cudaStream_t stream);

@@ -358,7 +358,7 @@ int run_syn_stream(int64_t rows, const void* a, const Level& L0, void* y, const 
     int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
     if (st != FDWT_OK) return st;
     int occ = 0;
-    FDWT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, SNT, smem));
+    if ((st = occupancy(reinterpret_cast<const void*>(kern), SNT, smem, &occ)) != FDWT_OK) return st;
     if (occ < 1) return FDWT_ERR_UNSUPPORTED;
     const int64_t grid = std::min<int64_t>(p.ntile, static_cast<int64_t>(occ) * sm_count());
     if (fill == kFillNone) {  // the tiles near the row ends on the tile kernel (same tile size)
@@ -656,7 +656,7 @@ int run_ana_stream(int64_t rows, const void* x, const Level& L0, void* a_out, co
     int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
     if (st != FDWT_OK) return st;
     int occ = 0;
-    FDWT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, SNT, smem));
+    if ((st = occupancy(reinterpret_cast<const void*>(kern), SNT, smem, &occ)) != FDWT_OK) return st;
     if (occ < 1) return FDWT_ERR_UNSUPPORTED;
     const int64_t grid = std::min<int64_t>(p.ntile, static_cast<int64_t>(occ) * sm_count());
     if ((st = pre_launch(stream)) != FDWT_OK) return st;

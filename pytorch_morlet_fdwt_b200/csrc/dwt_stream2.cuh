@@ -328,7 +328,7 @@ int run_ana2_stream(int64_t rows, const void* x, const Level& L1, const Level& L
     int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
     if (st != FDWT_OK) return st;
     int occ = 0;
-    FDWT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, SNT, pl.smem));
+    if ((st = occupancy(reinterpret_cast<const void*>(kern), SNT, pl.smem, &occ)) != FDWT_OK) return st;
     if (occ < 1) return FDWT_ERR_UNSUPPORTED;
     const int64_t grid = std::min<int64_t>(p.ntile, static_cast<int64_t>(occ) * sm_count());
     if ((st = pre_launch(stream)) != FDWT_OK) return st;
@@ -653,7 +653,7 @@ int run_syn2_stream(int64_t rows, const void* a2, const Level& Lc, const Level& 
     int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
     if (st != FDWT_OK) return st;
     int occ = 0;
-    FDWT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, SNT, pl.smem));
+    if ((st = occupancy(reinterpret_cast<const void*>(kern), SNT, pl.smem, &occ)) != FDWT_OK) return st;
     if (occ < 1) return FDWT_ERR_UNSUPPORTED;
     const int64_t grid = std::min<int64_t>(p.ntile, static_cast<int64_t>(occ) * sm_count());
     if ((st = pre_launch(stream)) != FDWT_OK) return st;

@@ -757,8 +757,13 @@ int run_syn_tiles(int64_t rows, const void* a, const std::vector<Level>& lv, voi
   for (auto it = fine.rbegin(); it != fine.rend(); ++it) stages.push_back(*it);
   const int ns = static_cast<int>(stages.size());
   if (ns == 1) {
-    if (ws_needed == nullptr && rows > 0)
+    if (ws_needed == nullptr && rows > 0) {
+      if (c == 0 && J == 2) {  // the whole synthesis is one fused pair
+        const int st = run_syn2_stream<T, LM>(rows, a, lv[0], lv[1], y, h0, h1, L, off, stream);
+        if (st != FDWT_ERR_UNSUPPORTED) return st;
+      }
       return run_syn_stage<T, LM>(rows, a, lv, y, h0, h1, L, off, stream);
+    }
     const int st = run_syn_tile_launch<T, LM>(rows, a, lv, y, h0, h1, L, off, stream,
                                               ws_needed != nullptr);
     if (st == FDWT_OK && ws_needed) *ws_needed = 0;

@@ -5,8 +5,9 @@ Same API and numbers as the reference's ``fdwt/dwt.py`` (``dwt``, ``idwt``, ``wa
 dimension and every leading dimension is a batch dimension.
 
 The reference launches one kernel per level from Python loops (``dwt.py:146-171``).  Here a
-whole multilevel transform is ONE autograd node and one fused launch
-(``fdwt_dwt_analysis`` / ``fdwt_dwt_synthesis`` in ``include/fdwt_b200.h``):
+whole multilevel transform is ONE autograd node and one C-ABI call
+(``fdwt_dwt_analysis`` / ``fdwt_dwt_synthesis`` in ``include/fdwt_b200.h``), which runs the
+levels as a short chain of streaming launches:
 
 * :class:`_AnalysisFn` -- multilevel analysis ``A``; its backward is :class:`_SynthesisFn`;
 * :class:`_SynthesisFn` -- the exact transpose ``A^T``; its backward is :class:`_AnalysisFn`.
@@ -20,6 +21,7 @@ two nodes are each other's backward, gradients of every order are available.
 
 from __future__ import annotations
 
+import functools
 from dataclasses import dataclass
 from typing import List, Optional, Sequence, Tuple
 
@@ -94,6 +96,14 @@ class _Spec:
         return self.coef_len[-1] + self.pad[-1]
 
 
+@functools.lru_cache(maxsize=512)
+def _spec_arrays(spec: _Spec):
+    """ctypes arrays of a spec's lengths and taps, built once per spec (the library only reads
+    them): (coef_len, pad, h0, h1, in_len)."""
+    return (_lib.i64_array(spec.coef_len), _lib.i64_array(spec.pad), _lib.f64_array(spec.h0),
+            _lib.f64_array(spec.h1), _lib.i64_array(spec.in_len))
+
+
 def _rows(t: torch.Tensor, n: int) -> torch.Tensor:
     return t.reshape(-1, n).contiguous()
 
@@ -108,7 +118,7 @@ def _analysis(x: torch.Tensor, spec: _Spec) -> List[torch.Tensor]:
     outs = [torch.empty((R, spec.approx_len), device=dev, dtype=x.dtype)]
     outs += [torch.empty((R, c), device=dev, dtype=x.dtype) for c in reversed(spec.coef_len)]
     J, L = spec.levels, len(spec.h0)
-    coef, pad = _lib.i64_array(spec.coef_len), _lib.i64_array(spec.pad)
+    coef, pad, h0, h1, _ = _spec_arrays(spec)
     dt = _lib.dtype_code(x.dtype)
     with torch.cuda.device(dev):
         nws = lib.fdwt_dwt_analysis_workspace(dt, R, spec.n, J, coef, pad, L, spec.mode,
@@ -116,7 +126,7 @@ def _analysis(x: torch.Tensor, spec: _Spec) -> List[torch.Tensor]:
         ws = _lib.workspace(nws, dev)
         st = lib.fdwt_dwt_analysis(
             dt, R, x2.data_ptr(), spec.n, J, coef, pad, _lib.ptr_array(outs),
-            _lib.f64_array(spec.h0), _lib.f64_array(spec.h1), L, spec.mode, spec.off,
+            h0, h1, L, spec.mode, spec.off,
             None if ws is None else ws.data_ptr(), nws, _lib.stream_of(dev))
     _lib.check(st, "fdwt_dwt_analysis")
     return [o.reshape(*lead, o.shape[-1]) for o in outs]
@@ -138,8 +148,7 @@ def _synthesis(inputs: Sequence[Optional[torch.Tensor]], spec: _Spec) -> torch.T
     if rows[0] is None:
         rows[0] = torch.zeros((R, spec.approx_len), device=dev, dtype=dtype)
     y = torch.empty((R, spec.n), device=dev, dtype=dtype)
-    coef = _lib.i64_array(spec.coef_len)
-    outl = _lib.i64_array(spec.in_len)
+    coef, _, h0, h1, outl = _spec_arrays(spec)
     dt = _lib.dtype_code(dtype)
     with torch.cuda.device(dev):
         nws = lib.fdwt_dwt_synthesis_workspace(dt, R, J, spec.approx_len, coef, outl, L,
@@ -147,7 +156,7 @@ def _synthesis(inputs: Sequence[Optional[torch.Tensor]], spec: _Spec) -> torch.T
         ws = _lib.workspace(nws, dev)
         st = lib.fdwt_dwt_synthesis(
             dt, R, J, _lib.ptr_array(rows), spec.approx_len, coef, outl, y.data_ptr(),
-            _lib.f64_array(spec.h0), _lib.f64_array(spec.h1), L, spec.mode, spec.off,
+            h0, h1, L, spec.mode, spec.off,
             None if ws is None else ws.data_ptr(), nws, _lib.stream_of(dev))
     _lib.check(st, "fdwt_dwt_synthesis")
     return y.reshape(*lead, spec.n)
