@@ -39,7 +39,7 @@ struct Ana2Params {
   int64_t P2;        // period of level k+1's boundary mode on n1
   int32_t n, nc1, n1, nc2, a_len2, off, mode, mode2, tiles;
   int32_t span;      // x elements per ring slot
-  int32_t T2;        // level-(k+1) outputs per tile (V q, with K1 = kh + 2q + kr <= SNT)
+  int32_t T2;        // level-(k+1) outputs per tile (V q, with K1 = kh + 2q + kr <= 2 SNT)
   int32_t K1, kh;    // level-k items per tile, of which kh before the first owned detail
   int32_t B, S2;     // buffer offset of the first level-k output; level-(k+1) window base
   int32_t abuf;      // buffer elements
@@ -244,8 +244,8 @@ Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int of
     const int NL = (R + W + VW - 1) / VW;
     const int kh = (-pmin + V - 1) / V;
     const int kr = (std::max(off - 1, 0) + V - 1) / V;
-    // one level-k item per thread: K1 = kh + T1 / V + kr <= SNT; then tiles of equal size
-    const int q_max = (SNT - kh - kr) / 2;
+    // two level-k items per thread: K1 = kh + T1 / V + kr <= 2 SNT; then tiles of equal size
+    const int q_max = (2 * SNT - kh - kr) / 2;
     const int64_t n_tiles = cdiv(nc2, static_cast<int64_t>(V) * q_max);
     const int T2 = V * static_cast<int>(cdiv(cdiv(nc2, n_tiles), V));
     const int T1 = 2 * T2;
