@@ -460,9 +460,21 @@ __device__ void syn2_tiles(const Syn2Params<A, LM>& p, A* ring, A* abuf, uint64_
       for (int m = tid; m < p.M1; m += SNT) {
         A z[2 * TQ];
         syn_window_item<A, LM, C0, R>(p.hp, a2s + 4 * m, d2s + 4 * m, z);
-        A* b = abuf + p.delta + 8 * m;
+        A* b = abuf + p.delta + 8 * m;  // vector stores (delta is even; the buffer is aligned)
+        if constexpr (sizeof(A) == 4) {
+          if ((p.delta & 3) == 0) {
+            reinterpret_cast<float4*>(b)[0] = make_float4(z[0], z[1], z[2], z[3]);
+            reinterpret_cast<float4*>(b)[1] = make_float4(z[4], z[5], z[6], z[7]);
+          } else {
 #pragma unroll
-        for (int q = 0; q < 2 * TQ; ++q) b[q] = z[q];
+            for (int q = 0; q < 2 * TQ; q += 2)
+              *reinterpret_cast<float2*>(b + q) = make_float2(z[q], z[q + 1]);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 2 * TQ; q += 2)
+            *reinterpret_cast<double2*>(b + q) = make_double2(z[q], z[q + 1]);
+        }
       }
     }
     __syncthreads();
