@@ -27,6 +27,11 @@
 namespace fdwt {
 namespace dwtk {
 
+// Ring slots of the fused analysis: fp32 needs three tiles in flight; fp64 tiles are as large
+// in bytes and run faster at three CTAs per SM with two slots (measured on B200).
+template <typename A>
+constexpr int ana2_stages() { return sizeof(A) == 8 ? 2 : 3; }
+
 template <typename A, int LM>
 struct Ana2Params {
   const A* x;        // (rows, n)
@@ -84,16 +89,16 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
     if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * n + lo, bytes, &bar[s]);
   };
 #pragma unroll 1
-  for (int s = 0; s < kStreamStages; ++s) {
+  for (int s = 0; s < ana2_stages<A>(); ++s) {
     const int64_t g = blockIdx.x + s * G;
     if (g < p.ntile) ext_fill(g, s);
     else cp_async_commit();
   }
-  cp_async_wait<kStreamStages - 1>();
+  cp_async_wait<ana2_stages<A>() - 1>();
   __syncthreads();
   if (tid == 0) {
 #pragma unroll 1
-    for (int s = 0; s < kStreamStages; ++s) {
+    for (int s = 0; s < ana2_stages<A>(); ++s) {
       const int64_t g = blockIdx.x + s * G;
       if (g < p.ntile) issue(g, s);
     }
@@ -101,8 +106,8 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
   int k = 0;
 #pragma unroll 1
   for (int64_t g = blockIdx.x; g < p.ntile; g += G, ++k) {
-    const int s = k % kStreamStages;
-    const unsigned par = static_cast<unsigned>(k / kStreamStages) & 1u;
+    const int s = k % ana2_stages<A>();
+    const unsigned par = static_cast<unsigned>(k / ana2_stages<A>()) & 1u;
     const bool ok = mbar_wait_bounded(&bar[s], par);
     const int64_t row = g / p.tiles;
     const int t = static_cast<int>(g % p.tiles);
@@ -155,23 +160,23 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
       if (t == p.tiles - 1 && tid == 0)
         for (int q = p.nc2; q < p.a_len2; ++q) a2row[q] = A(0);  // transpose of waverec's trim
     }
-    cp_async_wait<kStreamStages - 2>();  // this thread's gathers of tile k + 1
+    cp_async_wait<ana2_stages<A>() - 2>();  // this thread's gathers of tile k + 1
     if (__syncthreads_or(!ok)) {
       cp_async_wait<0>();
       if (tid == 0) {
         atomicExch(p.err, kErrCopyTimeout);
 #pragma unroll 1
-        for (int j = 0; j < kStreamStages; ++j) {
+        for (int j = 0; j < ana2_stages<A>(); ++j) {
           const int64_t gj = g + j * G;
           if (gj >= p.ntile) break;
           const int kj = k + j;
-          mbar_wait_bounded(&bar[kj % kStreamStages],
-                            static_cast<unsigned>(kj / kStreamStages) & 1u);
+          mbar_wait_bounded(&bar[kj % ana2_stages<A>()],
+                            static_cast<unsigned>(kj / ana2_stages<A>()) & 1u);
         }
       }
       return;
     }
-    const int64_t gn = g + kStreamStages * G;
+    const int64_t gn = g + ana2_stages<A>() * G;
     if (gn < p.ntile) {
       ext_fill(gn, s);
       if (tid == 0) issue(gn, s);
@@ -185,12 +190,12 @@ template <typename A, int LM>
 __global__ void __launch_bounds__(SNT, 2)
 dwt_ana2_stream_kernel(const __grid_constant__ Ana2Params<A, LM> p, int r) {
   extern __shared__ __align__(16) unsigned char ring_smem[];
-  __shared__ __align__(8) uint64_t bar[kStreamStages];
+  __shared__ __align__(8) uint64_t bar[ana2_stages<A>()];
   A* ring = reinterpret_cast<A*>(ring_smem);
-  A* abuf = ring + static_cast<size_t>(kStreamStages) * p.span;
+  A* abuf = ring + static_cast<size_t>(ana2_stages<A>()) * p.span;
   if (threadIdx.x == 0) {
 #pragma unroll
-    for (int s = 0; s < kStreamStages; ++s) mbar_init(&bar[s], 1);
+    for (int s = 0; s < ana2_stages<A>(); ++s) mbar_init(&bar[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
@@ -293,7 +298,7 @@ Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int of
     p.abuf = abuf;
     p.x_hi = static_cast<int>(std::min<int64_t>(2 * max_o1 + off + 1, 0x3fffffffLL));
     pl.R = R;
-    pl.smem = (static_cast<size_t>(kStreamStages) * span + abuf) * sizeof(A);
+    pl.smem = (static_cast<size_t>(ana2_stages<A>()) * span + abuf) * sizeof(A);
     pl.ok = pl.smem <= static_cast<size_t>(max_smem_optin()) - 2048;
     return pl;
   }
