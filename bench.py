@@ -44,8 +44,8 @@ FALLBACK_HBM_GBS = 6650.0
 # one ncu capture of each on 1024 of the 2048 rows scaled by 2 (traffic grows with the rows);
 # the captures are summarised in profiles/dwt_cfg2_kernels.txt
 TRAFFIC_PER_LAUNCH = {
-    "dwt_ana2_stream_kernel<float,16>": 980_400_000,
-    "dwt_syn2_stream_kernel<float,16,0>": 970_600_000,
+    "dwt_ana2_stream_kernel<float,16>": 974_800_000,
+    "dwt_syn2_stream_kernel<float,16,0>": 970_000_000,
 }
 
 
