@@ -148,7 +148,10 @@ __device__ __forceinline__ int block_size(int rem) {
 //   [3] sym(im)  = (h_im[c+k] + h_im[c-k]) / 2   (k = 0: h_im[c])
 // so that  re += [0] (xl + xr) + [2] (xl - xr),  im += [1] (xl - xr) + [3] (xl + xr)  exactly
 // reproduces sum_k h[c+k] x[n - dk] over k = -half..half of the octave.
-// build_coef returns (through flags[]) whether each block has nonzero [2]/[3] halves.
+// build_coef returns (through flags[]) whether each block has nonzero [2]/[3] halves, and
+// (through kmx[]) the last tap k of each block with a nonzero coefficient: the taps past it are
+// zero for every scale of the block (a scale's filter is shorter than the octave's widest), so
+// the STORE epilogue's tap loop stops there -- exact for any filter tensor.
 // fold_coef: folded coefficients of tap k of scale slot s, straight from the filter tensor.
 template <typename A>
 __device__ __forceinline__ void fold_coef(const FwdParams<A>& p, const Oct& O, int s, int k,
@@ -182,13 +185,16 @@ __device__ __forceinline__ void fold_coef(const FwdParams<A>& p, const Oct& O, i
 }
 
 template <typename A>
-__device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* flags) {
+__device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* flags, int* kmx) {
   const A* H = static_cast<const A*>(p.h);
   const int C = p.channels;
   const int hcols = 2 * p.center + 1;
   const int cnt = O.count, K = O.half;
   const int tid = threadIdx.x;
-  if (tid < 8) flags[tid] = 0;
+  if (tid < 8) {
+    flags[tid] = 0;
+    kmx[tid] = 0;
+  }
   __syncthreads();
   const bool in_smem = cnt * (K + 1) * 4 <= p.coef_cap;
   for (int w = tid; w < cnt * (K + 1); w += NT) {
@@ -202,13 +208,15 @@ __device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* fla
       d[2] = t[2];
       d[3] = t[3];
     }
-    if (t[2] != A(0) || t[3] != A(0)) {
+    const bool anti = t[2] != A(0) || t[3] != A(0);
+    if (anti || t[0] != A(0) || t[1] != A(0)) {
       int b = 0, s0 = 0;  // which block holds slot s
       while (s0 + block_size(cnt - s0) <= s) {
         s0 += block_size(cnt - s0);
         ++b;
       }
-      atomicOr(&flags[b], 1);
+      if (anti) atomicOr(&flags[b], 1);
+      if (k > 0) atomicMax(&kmx[b], k);
     }
   }
 }
@@ -218,9 +226,9 @@ __device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* fla
 template <typename A, int SB, bool SYM, bool GTAB>
 __device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
                                            const A* __restrict__ xb, int phi, int u0, int limit,
-                                           const A* __restrict__ tab, int s0,
+                                           const A* __restrict__ tab, int s0, int K,
                                            Acc2<A> (&acc)[SB][P]) {
-  const int ext = p.ext, dil = O.dil, K = O.half, cnt = O.count;
+  const int ext = p.ext, dil = O.dil, cnt = O.count;
   A L[P], R[P];
 #pragma unroll
   for (int i = 0; i < P; ++i) {
@@ -277,8 +285,8 @@ __device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
 // One block for one item, then its epilogue.
 template <typename T, typename A, int EPI, int SB, bool SYM>
 __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, const A* xb,
-                                         const A* tab, int s0, int phi, int u0, int64_t row,
-                                         A (&mix)[P], A (&sm_m)[P], A (&sm_l)[P],
+                                         const A* tab, int s0, int K, int phi, int u0,
+                                         int64_t row, A (&mix)[P], A (&sm_m)[P], A (&sm_l)[P],
                                          A (&sm_num)[P]) {
   const int64_t n = p.n;
   const int dil = O.dil;
@@ -286,9 +294,9 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
                                                        // the row end read clamped windows
   Acc2<A> acc[SB][P];
   if (O.count * (O.half + 1) * 4 <= p.coef_cap)
-    conv_block<A, SB, SYM, false>(p, O, xb, phi, u0, limit, tab, s0, acc);
+    conv_block<A, SB, SYM, false>(p, O, xb, phi, u0, limit, tab, s0, K, acc);
   else
-    conv_block<A, SB, SYM, true>(p, O, xb, phi, u0, limit, tab, s0, acc);
+    conv_block<A, SB, SYM, true>(p, O, xb, phi, u0, limit, tab, s0, K, acc);
   const int C = p.channels;
 #pragma unroll
   for (int s = 0; s < SB; ++s) {
@@ -360,24 +368,24 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
 
 template <typename T, typename A, int EPI, int SB>
 __device__ __forceinline__ void do_block_sym(const FwdParams<A>& p, const Oct& O, const A* xb,
-                                             const A* tab, int s0, bool sym, int phi, int u0,
+                                             const A* tab, int s0, int K, bool sym, int phi, int u0,
                                              int64_t row, A (&mix)[P], A (&sm_m)[P],
                                              A (&sm_l)[P], A (&sm_num)[P]) {
-  if (sym) do_block<T, A, EPI, SB, true>(p, O, xb, tab, s0, phi, u0, row, mix, sm_m, sm_l, sm_num);
-  else do_block<T, A, EPI, SB, false>(p, O, xb, tab, s0, phi, u0, row, mix, sm_m, sm_l, sm_num);
+  if (sym) do_block<T, A, EPI, SB, true>(p, O, xb, tab, s0, K, phi, u0, row, mix, sm_m, sm_l, sm_num);
+  else do_block<T, A, EPI, SB, false>(p, O, xb, tab, s0, K, phi, u0, row, mix, sm_m, sm_l, sm_num);
 }
 
 // Dispatch a block of runtime size 1..4.
 template <typename T, typename A, int EPI>
 __device__ __forceinline__ void run_block(const FwdParams<A>& p, const Oct& O, const A* xb,
-                                          const A* tab, int s0, int sb, bool sym, int phi,
-                                          int u0, int64_t row, A (&mix)[P], A (&sm_m)[P],
-                                          A (&sm_l)[P], A (&sm_num)[P]) {
+                                          const A* tab, int s0, int sb, int K, bool sym,
+                                          int phi, int u0, int64_t row, A (&mix)[P],
+                                          A (&sm_m)[P], A (&sm_l)[P], A (&sm_num)[P]) {
   switch (sb) {
-    case 1: do_block_sym<T, A, EPI, 1>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
-    case 2: do_block_sym<T, A, EPI, 2>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
-    case 3: do_block_sym<T, A, EPI, 3>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
-    default: do_block_sym<T, A, EPI, 4>(p, O, xb, tab, s0, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    case 1: do_block_sym<T, A, EPI, 1>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    case 2: do_block_sym<T, A, EPI, 2>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    case 3: do_block_sym<T, A, EPI, 3>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    default: do_block_sym<T, A, EPI, 4>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
   }
 }
 
@@ -417,6 +425,7 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   A* tab = reinterpret_cast<A*>(smem + p.coef_off);
   A* extra = reinterpret_cast<A*>(smem + p.extra_off);
   __shared__ int flags[8];
+  __shared__ int kmx[8];  // per scale block: last tap with a nonzero coefficient
   const int64_t row = blockIdx.x;
   const int n = static_cast<int>(p.n);
   const int ext = p.ext;
@@ -443,7 +452,7 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   for (int j = 0; j < p.n_oct; ++j) {
     const Oct& O = p.oct[j];
     if (O.count > 0) {
-      build_coef<A>(p, O, tab, flags);
+      build_coef<A>(p, O, tab, flags, kmx);
       __syncthreads();
       const int dil = O.dil;
       const int runs = (static_cast<int>((p.n + dil - 1) / dil) + P - 1) / P;
@@ -459,7 +468,8 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
           const int phi = it % dil, u0 = (it / dil) * P;
           if (phi >= n) continue;
           A mix[P], m_[P], l_[P], num_[P];
-          run_block<T, A, EPI>(p, O, cur, tab, s0, block_size(O.count - s0), flags[blk] == 0,
+          run_block<T, A, EPI>(p, O, cur, tab, s0, block_size(O.count - s0), kmx[blk],
+                               flags[blk] == 0,
                                phi, u0, row, mix, m_, l_, num_);
         }
       } else {
@@ -484,7 +494,9 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
           int s0 = 0;
           for (int b = 0; b < nblk; ++b) {
             const int sb = block_size(O.count - s0);
-            run_block<T, A, EPI>(p, O, cur, tab, s0, sb, flags[b] == 0, phi, u0, row, mix,
+            // (the fused epilogues keep the octave's full tap range: the per-block limit made
+            // the mix and softmax kernels slower on B200, 2.04 -> 2.50 ms on cfg4)
+            run_block<T, A, EPI>(p, O, cur, tab, s0, sb, O.half, flags[b] == 0, phi, u0, row, mix,
                                  sm_m, sm_l, sm_num);
             s0 += sb;
           }
