@@ -144,11 +144,17 @@ __device__ __forceinline__ A block_sum(A v, A* red) {
 
 // Folded taps of every scale of an octave (k = 0..K), as in the forward's coefficient table:
 // tab[(s * (K + 1) + k) * 4 + c]; sym[s] = 1 when the scale's antisymmetric-real /
-// symmetric-imaginary halves are all zero (exactly symmetric filter).  Ends with a barrier.
+// symmetric-imaginary halves are all zero (exactly symmetric filter); klast[s] = the last tap k
+// of the scale with a nonzero coefficient (the octave's table spans its widest filter; past
+// klast[s] the scale's taps are zero, so its adjoint stops there).  Ends with a barrier.
 template <typename A>
-__device__ void build_octave_taps(const FwdParams<A>& f, const Oct& O, A* tab, int* sym) {
+__device__ void build_octave_taps(const FwdParams<A>& f, const Oct& O, A* tab, int* sym,
+                                  int* klast) {
   const int K1 = O.half + 1;
-  for (int s = threadIdx.x; s < O.count; s += NT) sym[s] = 1;
+  for (int s = threadIdx.x; s < O.count; s += NT) {
+    sym[s] = 1;
+    klast[s] = 0;
+  }
   __syncthreads();
   for (int w = threadIdx.x; w < O.count * K1; w += NT) {
     const int s = w / K1, k = w - s * K1;
@@ -160,6 +166,8 @@ __device__ void build_octave_taps(const FwdParams<A>& f, const Oct& O, A* tab, i
     d[2] = t[2];
     d[3] = t[3];
     if (t[2] != A(0) || t[3] != A(0)) sym[s] = 0;
+    if (k > 0 && (t[0] != A(0) || t[1] != A(0) || t[2] != A(0) || t[3] != A(0)))
+      atomicMax(&klast[s], k);
   }
   __syncthreads();
 }
@@ -309,9 +317,9 @@ __device__ __forceinline__ void adjoint_taps(const A* tab, const A* gw, int n, i
 // whole window lies in [-1, n] skip the per-load clamp.
 template <typename A, int C, bool SYM>
 __device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab, const A* gw,
-                              A* G, int pa, int pb) {
+                              A* G, int pa, int pb, int K) {
   const int n = static_cast<int>(f.n);
-  const int dil = O.dil, K = O.half;
+  const int dil = O.dil;
   const int len = pb - pa;
   if (len <= 0) return;
   const int runs = static_cast<int>(cdiv(cdiv(len, dil), P));
@@ -503,11 +511,11 @@ __device__ void make_gw(const BwdParams<A>& p, const Oct& O, int s, int gs, cons
 template <typename A, int C, bool SYM>
 __device__ __forceinline__ void scale_grads(const BwdParams<A>& p, const Oct& O, int live, int gs,
                                             A* G, const A* X, const A* gw, const A* tab,
-                                            int64_t row) {
+                                            int64_t row, int ks) {
   const FwdParams<A>& f = p.f;
-  if (p.need_gx) {
-    const int reach = min(live, O.half * O.dil);
-    adjoint_scale<A, C, SYM>(f, O, tab, gw, G, -reach, static_cast<int>(f.n) + reach);
+  if (p.need_gx) {  // the adjoint over the scale's nonzero taps (ks <= O.half) and their reach
+    const int reach = min(live, ks * O.dil);
+    adjoint_scale<A, C, SYM>(f, O, tab, gw, G, -reach, static_cast<int>(f.n) + reach, ks);
   }
   if (p.gh_part) {
     const int hcols = 2 * f.center + 1;
@@ -518,7 +526,7 @@ __device__ __forceinline__ void scale_grads(const BwdParams<A>& p, const Oct& O,
 // MIX / SOFTMAX: dL/dW of each scale is formed from the recomputed W (make_gw) into one buffer.
 template <typename A, int EPI, int C, bool SYM>
 __device__ void scale_pass(const BwdParams<A>& p, const Oct& O, int live, int s, A* G,
-                           const A* X, A* gw, const A* tab, A* red, int64_t row) {
+                           const A* X, A* gw, const A* tab, A* red, int64_t row, int ks) {
   const FwdParams<A>& f = p.f;
   const int gs = f.order[O.begin + s];
   A sa = A(0), sb = A(0);
@@ -535,7 +543,7 @@ __device__ void scale_pass(const BwdParams<A>& p, const Oct& O, int live, int s,
     if (threadIdx.x == 0) p.v_part[row * f.n_scales + gs] = ta;
   }
   __syncthreads();
-  scale_grads<A, C, SYM>(p, O, live, gs, G, X, gw, tab, row);
+  scale_grads<A, C, SYM>(p, O, live, gs, G, X, gw, tab, row, ks);
   __syncthreads();
 }
 
@@ -543,11 +551,13 @@ __device__ void scale_pass(const BwdParams<A>& p, const Oct& O, int live, int s,
 // loading while scale s is processed (the first one was issued by the caller).
 template <typename A, int EPI, int C>
 __device__ void octave_pass(const BwdParams<A>& p, const Oct& O, int live, A* G, const A* X,
-                            A* const* gws, const A* tab, const int* sym, A* red, int64_t row) {
+                            A* const* gws, const A* tab, const int* sym, const int* klast,
+                            A* red, int64_t row) {
   const int K1 = O.half + 1;
   for (int s = 0; s < O.count; ++s) {
     const A* ts = tab + 4 * K1 * s;
     const bool sy = sym[s] != 0;
+    const int ks = klast[s];
     if (EPI == EPI_STORE) {
       if (s + 1 < O.count) {
         stage_gw<A, C>(p, p.f.order[O.begin + s + 1], row, gws[(s + 1) & 1]);
@@ -558,12 +568,12 @@ __device__ void octave_pass(const BwdParams<A>& p, const Oct& O, int live, A* G,
       }
       __syncthreads();
       const int gs = p.f.order[O.begin + s];
-      if (sy) scale_grads<A, C, true>(p, O, live, gs, G, X, gws[s & 1], ts, row);
-      else scale_grads<A, C, false>(p, O, live, gs, G, X, gws[s & 1], ts, row);
+      if (sy) scale_grads<A, C, true>(p, O, live, gs, G, X, gws[s & 1], ts, row, ks);
+      else scale_grads<A, C, false>(p, O, live, gs, G, X, gws[s & 1], ts, row, ks);
       __syncthreads();
     } else {
-      if (sy) scale_pass<A, EPI, C, true>(p, O, live, s, G, X, gws[0], ts, red, row);
-      else scale_pass<A, EPI, C, false>(p, O, live, s, G, X, gws[0], ts, red, row);
+      if (sy) scale_pass<A, EPI, C, true>(p, O, live, s, G, X, gws[0], ts, red, row, ks);
+      else scale_pass<A, EPI, C, false>(p, O, live, s, G, X, gws[0], ts, red, row, ks);
     }
   }
 }
@@ -579,6 +589,7 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
   A* tab = reinterpret_cast<A*>(smem + p.tab_off);
   A* red = reinterpret_cast<A*>(smem + p.red_off);
   __shared__ int sym[kMaxScales];
+  __shared__ int klast[kMaxScales];  // per scale of the octave: last nonzero tap
   const int64_t row = blockIdx.x;
   const int n = static_cast<int>(f.n);
   const int E = f.ext;
@@ -640,9 +651,11 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
           atE(f, X, q) = (q >= -lv && q < n + lv) ? srcp[q + lv] : A(0);
       }
       __syncthreads();
-      build_octave_taps<A>(f, O, tab, sym);
-      if (f.channels == 2) octave_pass<A, EPI, 2>(p, O, O.live, G, X, gws, tab, sym, red, row);
-      else octave_pass<A, EPI, 1>(p, O, O.live, G, X, gws, tab, sym, red, row);
+      build_octave_taps<A>(f, O, tab, sym, klast);
+      if (f.channels == 2)
+        octave_pass<A, EPI, 2>(p, O, O.live, G, X, gws, tab, sym, klast, red, row);
+      else
+        octave_pass<A, EPI, 1>(p, O, O.live, G, X, gws, tab, sym, klast, red, row);
     }
   }
   __syncthreads();
