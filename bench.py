@@ -1,34 +1,37 @@
 #!/usr/bin/env python
 """Benchmark of the wavelet filter-bank hot path on B200 (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config all|cfg1|cfg2|cfg3|cfg3l|cfg4|cfg5|cfg5c]
 
-Default workload (configs[1] of the baseline, the one the headline metric is quoted on):
-db8 ``periodization`` level-8 ``wavedec`` of x float32 (16, 128, 65536) i.i.d. N(0,1), ``waverec``
-of the coefficients, and the autograd backward through both.  One step = those four
-multilevel transforms over the whole batch (each a chain of streaming launches, two levels
-per launch where the shapes allow);
-inputs (512 MiB per array) are larger than the 126 MB L2.
+Headline (configs[1] of the baseline, the one the metric is quoted on): db8 ``periodization``
+level-8 ``wavedec`` of x float32 (16, 128, 65536) i.i.d. N(0,1), ``waverec`` of the
+coefficients, and the autograd backward through both.  One step = those four multilevel
+transforms over the whole batch; arrays of 512 MiB, larger than the 126 MB L2.  ``value`` is the
+whole-job algorithmic HBM throughput in GB/s (unique bytes the four transforms must read and
+write), device-timed with CUDA events over K steps, max over ranks.  Each rank runs the full
+config on its own data ("weak" scaling: rows shard with no collective); at N > 1 the line also
+carries ``strong_scaling`` (the config's batch split over the ranks) and ``gather`` (the
+optional NCCL all-gather of the per-rank results, timed apart).
 
-``value`` is the whole-job algorithmic HBM throughput in GB/s (unique bytes the four transforms
-must read and write: inputs once, outputs once), device-timed with CUDA events over K steps,
-max over ranks.  Each rank runs the full config on its own data ("weak" scaling: the path
-shards by rows and has no collective).  ``e2e`` repeats the step through the public API with
-the input in pinned host memory and the gradient copied back every step.
+The same line carries ``configs``: every other baseline config (cfg1, cfg3, cfg3 learnable,
+cfg4, cfg5 and its channel-mix variant), each measured the same way with its own roofline
+(HBM bytes, or FP32 FMA work for the fused mixers), ``e2e`` and CPU baseline.
 
-``--impl reference`` times the reference algorithm's CPU path (the oracle port in ``oracle/``,
-restating the reference's own CPU code) on the host cores, on a bounded row sample per step.
+CPU baseline and the reference arm (``--impl reference``): the reference package's own CPU
+PyTorch path (``fdwt`` installed under ``baseline/_ref``, called with CPU tensors, all host
+threads), on a bounded sample of each workload (rows or batch entries: the ops are row-wise, so
+the sample's per-unit cost is the workload's).  Without ``baseline/_ref`` the oracle port in
+``oracle/`` stands in and ``kind`` says "port".
 """
 
 from __future__ import annotations
 
 import argparse
+import importlib
 import json
-import math
-import multiprocessing as mp
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -47,6 +50,7 @@ TRAFFIC_PER_LAUNCH = {
     "dwt_ana2_stream_kernel<float,16>": 974_800_000,
     "dwt_syn2_stream_kernel<float,16,0>": 970_000_000,
 }
+CONFIG_NAMES = ["cfg1", "cfg3", "cfg3l", "cfg4", "cfg5", "cfg5c"]
 
 
 # ------------------------------------------------------------------------------ helpers
@@ -58,6 +62,31 @@ def peaks():
             p = json.load(f)
         return float(p["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def fp32_fma_peak(dev):
+    """FP32 (non-tensor) peak of this GPU, measured: cuBLAS SGEMM 8192^3 with TF32 off, best
+    of 5 (GFLOP/s).  The denominator of the fused mixers' FMA roofline."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev)
+        b = torch.randn(n, n, device=dev)
+        c = a @ b
+        best = float("inf")
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b, c
+        return 2.0 * n ** 3 / (best / 1e3) / 1e9
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 class ClockSampler:
@@ -138,172 +167,610 @@ def job_throughput(units_per_rank_step, steps, world, ms, scale=1.0):
     return units_per_rank_step * steps * world / (ms / 1e3) / scale
 
 
-# ------------------------------------------------------------------------------ workload
-
-CFG2 = dict(shape=(16, 128, 65536), wavelet="db8", mode="periodization", level=8)
-
-
-def cfg2_bytes_per_row():
-    """Algorithmic bytes of one row through the four launches of a step (fp32)."""
-    from oracle.dwt_oracle import dwt_coeff_len
-    n = CFG2["shape"][-1]
-    lens, cur = [], n
-    for _ in range(CFG2["level"]):
-        cur = dwt_coeff_len(cur, 16, CFG2["mode"])
-        lens.append(cur)
-    coef = sum(lens) + lens[-1]
-    per_dir = (n + coef) * 4  # read one side, write the other
-    return 4 * per_dir, per_dir
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
-def _cpu_rows_task(args):
-    """One worker: the full step on a chunk of rows, with the oracle (fp32)."""
-    rows, seed = args
-    from oracle import dwt_oracle as D
+# ------------------------------------------------------------------------------ CPU baselines
+
+_REF = None
+
+
+def reference_package():
+    """The reference package (import name ``fdwt``) installed under ``baseline/_ref``, or None.
+    Its CPU path runs when it is given CPU tensors."""
+    global _REF
+    if _REF is None:
+        path = os.path.join(ROOT, "baseline", "_ref")
+        _REF = False
+        if os.path.isdir(os.path.join(path, "fdwt")):
+            sys.path.insert(0, path)
+            try:
+                _REF = importlib.import_module("fdwt")
+            except Exception:
+                _REF = False
+            finally:
+                sys.path.remove(path)
+    return _REF or None
+
+
+def _explicit_bank(name):
+    """(dec_lo, dec_hi, rec_lo, rec_hi) lists of a Daubechies bank: PyWavelets (which the
+    reference needs for names) is absent, so both packages get the same explicit bank."""
     from pytorch_morlet_fdwt_b200.wavelets import get_filter_bank
-    b = get_filter_bank(CFG2["wavelet"])
-    tb = (b.dec_lo, b.dec_hi, b.rec_lo, b.rec_hi)
-    x = np.random.default_rng(seed).standard_normal((rows, CFG2["shape"][-1])).astype(np.float32)
-    t = time.perf_counter()
-    c = D.wavedec(x, tb, CFG2["mode"], CFG2["level"])
-    y = D.waverec(c, tb, CFG2["mode"])
-    gc = D.waverec_vjp(c, y, tb, CFG2["mode"])
-    D.wavedec_vjp(x.shape[-1], gc, tb, CFG2["mode"])
-    return time.perf_counter() - t
+    b = get_filter_bank(name)
+    return (list(b.dec_lo), list(b.dec_hi), list(b.rec_lo), list(b.rec_hi))
 
 
-class CpuPool:
-    """Spawned worker pool for the CPU oracle (created before any CUDA call)."""
-
-    def __init__(self, cores: int):
-        self.cores = cores
-        self.pool = mp.get_context("spawn").Pool(cores)
-        self.pool.map(_cpu_rows_task, [(2, 0)] * cores)  # import + operator caches warm
-
-    def step(self, rows: int) -> float:
-        per = max(1, rows // self.cores)
-        t = time.perf_counter()
-        self.pool.map(_cpu_rows_task, [(per, i) for i in range(self.cores)])
-        return time.perf_counter() - t, per * self.cores
-
-    def close(self):
-        self.pool.close()
-        self.pool.join()
-
-
-def cpu_sample(pool: CpuPool, rows: int, reps: int):
+def cpu_time(fn, reps):
+    """Median wall time of `reps` calls of fn() after one warm-up call."""
+    fn()
     times = []
-    done = rows
     for _ in range(reps):
-        t, done = pool.step(rows)
-        times.append(t)
-    t = statistics.median(times)
-    step_bytes, _ = cfg2_bytes_per_row()
-    return step_bytes * done / t / 1e9, t, done
+        t = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t)
+    return statistics.median(times), times
 
 
-# ------------------------------------------------------------------------------ our arm
+# ------------------------------------------------------------------------------ workloads
+#
+# A workload knows its GPU step (forward + backward, split for timing), its dominant kernel
+# (timed alone for the roofline), its algorithmic units, and the reference CPU path on a
+# bounded sample.  `batch` is the number of batch entries a rank runs (the config's, or its
+# share under strong scaling).
 
-def run_ours(args, rank, world, local_rank, pool):
-    import torch
-    import torch.distributed as dist
-    import pytorch_morlet_fdwt_b200 as F
-    from pytorch_morlet_fdwt_b200 import _lib
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    torch.manual_seed(1234 + rank)
-    shape = CFG2["shape"]
-    if args.rows is not None:
-        shape = (1, args.rows, shape[-1])
-    bank = F.get_filter_bank(CFG2["wavelet"])
-    mode, level = CFG2["mode"], CFG2["level"]
-    x0 = torch.randn(shape, device=dev)
-    R = shape[0] * shape[1]
-    step_bytes_row, dir_bytes_row = cfg2_bytes_per_row()
-    step_bytes = step_bytes_row * R
-    gy = torch.randn(shape, device=dev)
+def _dwt_lens(n, L, mode, level):
+    from pytorch_morlet_fdwt_b200.dwt import dwt_coeff_len
+    lens, cur = [], n
+    for _ in range(level):
+        cur = dwt_coeff_len(cur, L, mode)
+        lens.append(cur)
+    return lens
 
-    def step(x):
-        coeffs = F.wavedec(x, bank, mode, level)
-        y = F.waverec(coeffs, bank, mode)
+
+def _fma_per_position(plan):
+    """Algorithmic FMAs of one forward filter-bank pass per signal position: a complex scale
+    with half-support c costs 2c + 1 FMAs after folding the even real and odd imaginary taps
+    (one FMA per tap pair for each of re and im, plus the centre)."""
+    return sum(2 * c + 1 for st in plan.stages for c in st.support)
+
+
+class Workload:
+    key = ""
+    unit = "GB/s"
+    batch = 1
+    dtype = "f32"
+
+    def units(self, batch):            # algorithmic units of one step on `batch` entries
+        raise NotImplementedError
+
+    def setup(self, dev, batch):
+        raise NotImplementedError
+
+    def fwd(self, st):
+        raise NotImplementedError
+
+    def bwd(self, st):
+        pass
+
+    def e2e_step(self, st, x):         # full step on an uploaded input; returns the download
+        raise NotImplementedError
+
+    def kernel(self, st):              # (name, callable running the dominant kernel once,
+        raise NotImplementedError      #  algorithmic work per call, "hbm" | "fma")
+
+    def cpu(self, ref, sample):        # seconds of the CPU path on `sample` entries
+        raise NotImplementedError
+
+    cpu_sample = 1
+    cpu_sample_unit = "batch entries"
+
+
+class Cfg2(Workload):
+    key = "cfg2"
+    batch = 16
+    shape = (128, 65536)
+    wavelet, mode, level = "db8", "periodization", 8
+    name = ("cfg2: db8 periodization level-8 wavedec + waverec + backward through both, x "
+            "float32 (16, 128, 65536)")
+    cpu_sample = 64
+    cpu_sample_unit = "rows"
+
+    def dir_bytes_per_row(self):
+        n = self.shape[-1]
+        lens = _dwt_lens(n, 16, self.mode, self.level)
+        return (n + sum(lens) + lens[-1]) * 4
+
+    def units(self, batch):
+        return 4 * self.dir_bytes_per_row() * batch * self.shape[0]
+
+    def setup(self, dev, batch, rows=None):
+        import torch
+        import pytorch_morlet_fdwt_b200 as F
+        shape = (batch,) + self.shape if rows is None else (1, rows, self.shape[-1])
+        st = {"bank": F.get_filter_bank(self.wavelet), "F": F}
+        st["x"] = torch.randn(shape, device=dev).requires_grad_()
+        st["gy"] = torch.randn(shape, device=dev)
+        return st
+
+    def fwd(self, st):
+        F = st["F"]
+        st["c"] = F.wavedec(st["x"], st["bank"], self.mode, self.level)
+        st["y"] = F.waverec(st["c"], st["bank"], self.mode)
+
+    def bwd(self, st):
+        import torch
+        st["x"].grad = None
+        torch.autograd.backward(st["y"], st["gy"])
+
+    def e2e_step(self, st, x):
+        import torch
+        F = st["F"]
+        y = F.waverec(F.wavedec(x, st["bank"], self.mode, self.level), st["bank"], self.mode)
+        torch.autograd.backward(y, st["gy"])
+        return x.grad
+
+    def kernels(self, st):
+        """The two finest levels of the step's analysis / synthesis in one launch each."""
+        F = st["F"]
+        x2 = st["x"].detach().reshape(-1, self.shape[-1])
+        c2 = F.wavedec(x2, st["bank"], self.mode, 2)
+        return {"dwt_ana2_stream_kernel<float,16>":
+                lambda: F.wavedec(x2, st["bank"], self.mode, 2),
+                "dwt_syn2_stream_kernel<float,16,0>":
+                lambda: F.waverec(c2, st["bank"], self.mode)}
+
+    def cpu(self, ref, sample):
+        import torch
+        if ref is None:
+            from oracle import dwt_oracle as D
+            tb = _explicit_bank(self.wavelet)
+            x = np.random.default_rng(0).standard_normal((sample, self.shape[-1])).astype(
+                np.float32)
+            t = time.perf_counter()
+            c = D.wavedec(x, tb, self.mode, self.level)
+            y = D.waverec(c, tb, self.mode)
+            gc = D.waverec_vjp(c, y, tb, self.mode)
+            D.wavedec_vjp(x.shape[-1], gc, tb, self.mode)
+            return time.perf_counter() - t
+        bank = _explicit_bank(self.wavelet)
+        x = torch.randn(sample, self.shape[-1], requires_grad=True)
+        gy = torch.randn(sample, self.shape[-1])
+        t = time.perf_counter()
+        y = ref.waverec(ref.wavedec(x, bank, self.mode, self.level), bank, self.mode)
         torch.autograd.backward(y, gy)
+        return time.perf_counter() - t
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    def cpu_units(self, sample):
+        return 4 * self.dir_bytes_per_row() * sample
 
-    x = x0.clone().requires_grad_()
-    for _ in range(args.warmup):
-        x.grad = None
-        step(x)
+
+class Cfg1(Workload):
+    key = "cfg1"
+    batch = 32
+    shape = (64, 2500)
+    name = ("cfg1: db4 symmetric level-5 wavedec, its backward of sum(coeffs^2), and waverec, "
+            "x float32 (32, 64, 2500)")
+    cpu_sample = 32
+
+    def dir_bytes_per_row(self):
+        n = self.shape[-1]
+        lens = _dwt_lens(n, 8, "symmetric", 5)
+        return (n + sum(lens) + lens[-1]) * 4
+
+    def units(self, batch):
+        return 3 * self.dir_bytes_per_row() * batch * self.shape[0]
+
+    def setup(self, dev, batch):
+        import torch
+        import pytorch_morlet_fdwt_b200 as F
+        return {"F": F, "bank": F.get_filter_bank("db4"),
+                "x": torch.randn((batch,) + self.shape, device=dev).requires_grad_()}
+
+    def fwd(self, st):
+        F = st["F"]
+        st["c"] = F.wavedec(st["x"], st["bank"], "symmetric", 5)
+        st["y"] = F.waverec([c.detach() for c in st["c"]], st["bank"], "symmetric")
+
+    def bwd(self, st):
+        st["x"].grad = None
+        sum(c.square().sum() for c in st["c"]).backward()
+
+    def e2e_step(self, st, x):
+        F = st["F"]
+        c = F.wavedec(x, st["bank"], "symmetric", 5)
+        st["y"] = F.waverec([v.detach() for v in c], st["bank"], "symmetric")
+        sum(v.square().sum() for v in c).backward()
+        return x.grad
+
+    def kernel(self, st):
+        F = st["F"]
+        return ("wavedec call: dwt_analysis_kernel<float> (all five levels in one launch)",
+                lambda: F.wavedec(st["x"].detach(), st["bank"], "symmetric", 5),
+                self.dir_bytes_per_row() * st["x"].shape[0] * self.shape[0], "hbm")
+
+    def cpu(self, ref, sample):
+        import torch
+        bank = _explicit_bank("db4")
+        mod = ref if ref is not None else None
+        x = torch.randn((sample,) + self.shape, requires_grad=True)
+        if mod is None:
+            from oracle import dwt_oracle as D
+            xn = x.detach().reshape(-1, self.shape[-1]).numpy()
+            t = time.perf_counter()
+            c = D.wavedec(xn, bank, "symmetric", 5)
+            D.waverec(c, bank, "symmetric")
+            D.wavedec_vjp(self.shape[-1], [2 * v for v in c], bank, "symmetric")
+            return time.perf_counter() - t
+        t = time.perf_counter()
+        c = mod.wavedec(x, bank, "symmetric", 5)
+        mod.waverec([v.detach() for v in c], bank, "symmetric")
+        sum(v.square().sum() for v in c).backward()
+        return time.perf_counter() - t
+
+    def cpu_units(self, sample):
+        return self.units(sample)
+
+
+class Cfg3(Workload):
+    batch = 32
+    shape = (64, 2500)
+
+    def __init__(self, learnable):
+        self.learnable = learnable
+        self.key = "cfg3l" if learnable else "cfg3"
+        self.name = ("cfg3: Morlet CWT fast, 40 freqs logspace(-0.3,2) @ 250 Hz, l1, x float32 "
+                     "(32, 64, 2500) -> complex64 (32, 64, 40, 2500)")
+        if learnable:
+            self.name += "; learnable scales and w0, forward + backward of sum |W|^2"
+        self.cpu_sample = 1 if learnable else 4
+
+    def _bytes(self, batch):
+        rows = batch * self.shape[0]
+        x = rows * self.shape[1] * 4
+        w = rows * 40 * self.shape[1] * 8
+        return x, w
+
+    def units(self, batch):
+        x, w = self._bytes(batch)
+        return x + w + (w + 2 * x if self.learnable else 0)
+
+    def _module(self, F):
+        return F.CWT1D(freqs=np.logspace(-0.3, 2, 40), fs=250.0, norm="l1",
+                       learnable=self.learnable, learnable_w0=self.learnable)
+
+    def setup(self, dev, batch):
+        import torch
+        import pytorch_morlet_fdwt_b200 as F
+        torch.manual_seed(0)
+        m = self._module(F).to(dev)
+        return {"m": m, "x": torch.randn((batch,) + self.shape,
+                                         device=dev).requires_grad_(self.learnable)}
+
+    def fwd(self, st):
+        st["y"] = st["m"](st["x"])
+
+    def bwd(self, st):
+        import torch
+        if self.learnable:
+            st["x"].grad = None
+            st["m"].zero_grad()
+            torch.view_as_real(st["y"]).square().sum().backward()
+
+    def e2e_step(self, st, x):
+        import torch
+        if not self.learnable:
+            return torch.view_as_real(st["m"](x.detach()))
+        st["m"].zero_grad()
+        torch.view_as_real(st["m"](x)).square().sum().backward()
+        return x.grad
+
+    def kernel(self, st):
+        import torch
+        from pytorch_morlet_fdwt_b200.cwt import _cwt_backward, _cwt_forward
+        m = st["m"]
+        x2 = st["x"].detach().reshape(-1, self.shape[1])
+        H = m._filters(x2.device, torch.float32).detach()
+        xb, wb = self._bytes(st["x"].shape[0])
+        if not self.learnable:
+            return ("cwt_forward_kernel<float,float,0>", lambda: _cwt_forward(x2, m.plan, H),
+                    xb + wb, "hbm")
+        g = torch.randn((x2.shape[0], 40, self.shape[1], 2), device=x2.device)
+        return ("cwt_backward_kernel<float,0> + reduce_rows_kernel (dL/dx and dL/dH)",
+                lambda: _cwt_backward(g, x2, m.plan, H, True, True), wb + 2 * xb, "hbm")
+
+    def cpu(self, ref, sample):
+        import torch
+        x = torch.randn((sample,) + self.shape, requires_grad=self.learnable)
+        if ref is None:
+            import pytorch_morlet_fdwt_b200 as F
+            from oracle import cwt_oracle as C
+            m = self._module(F)
+            po = C.Plan(m.plan.scales, norm="l1", support_margin=1.25 if self.learnable else 1.0)
+            ls = m.log_scales.detach().double().requires_grad_(self.learnable)
+            w0 = torch.tensor(6.0, dtype=torch.float64, requires_grad=self.learnable)
+            t = time.perf_counter()
+            W = C.apply_plan(x.detach().double().requires_grad_(self.learnable), po,
+                             po.filters(ls.exp(), w0))
+            if self.learnable:
+                W.abs().square().sum().backward()
+            return time.perf_counter() - t
+        m = self._module(ref)
+        t = time.perf_counter()
+        W = m(x)
+        if self.learnable:
+            torch.view_as_real(W).square().sum().backward()
+        return time.perf_counter() - t
+
+    def cpu_units(self, sample):
+        return self.units(sample)
+
+
+class Cfg4(Workload):
+    key = "cfg4"
+    unit = "tokens/s"
+    batch = 8
+    shape = (4096, 256)
+    name = ("cfg4: MorletTokenMixer dim 256, 16 freqs logspace(0,1.8) @ 250 Hz, x float32 "
+            "(8, 4096, 256), forward + backward of sum(y^2)")
+
+    def units(self, batch):
+        return batch * self.shape[0]
+
+    def _module(self, F):
+        import torch
+        torch.manual_seed(0)
+        return F.MorletTokenMixer(256, freqs=np.logspace(0, 1.8, 16).tolist(), fs=250)
+
+    def setup(self, dev, batch):
+        import torch
+        import pytorch_morlet_fdwt_b200 as F
+        m = self._module(F).to(dev)
+        return {"m": m, "x": torch.randn((batch,) + self.shape, device=dev).requires_grad_()}
+
+    def fwd(self, st):
+        st["y"] = st["m"](st["x"])
+
+    def bwd(self, st):
+        st["x"].grad = None
+        st["m"].zero_grad()
+        st["y"].square().sum().backward()
+
+    def e2e_step(self, st, x):
+        st["m"].zero_grad()
+        st["m"](x).square().sum().backward()
+        return x.grad
+
+    def kernel(self, st):
+        import torch
+        from pytorch_morlet_fdwt_b200.cwt import _mix_backward
+        m = st["m"]
+        B = st["x"].shape[0]
+        x2 = st["x"].detach().transpose(1, 2).reshape(-1, self.shape[0]).contiguous()
+        H = m.cwt._filters(x2.device, torch.float32).detach()
+        gy = torch.randn_like(x2)
+        a, b = m.mag_weight.detach(), m.phase_weight.detach()
+        fma = 3 * _fma_per_position(m.cwt.plan) * x2.numel()
+        return ("cwt_backward_kernel<float,1> + reduce_rows_kernel (mix backward: recompute, "
+                "adjoint, filter gradient)",
+                lambda: _mix_backward(gy, x2, m.cwt.plan, H, a, b, True, True), fma, "fma")
+
+    def cpu(self, ref, sample):
+        import torch
+        x = torch.randn((sample,) + self.shape, requires_grad=True)
+        if ref is None:
+            import pytorch_morlet_fdwt_b200 as F
+            from oracle import cwt_oracle as C
+            m = self._module(F).double()
+            po = C.Plan(m.cwt.plan.scales, support_margin=1.25)
+            ls = m.cwt.log_scales.detach().double().requires_grad_()
+            xd = x.detach().double().requires_grad_()
+            t = time.perf_counter()
+            y = C.token_mixer(xd, po, po.filters(ls.exp(), m.cwt.w0_value), m.mag_weight,
+                              m.phase_weight, m.bias, m.out_proj.weight, m.out_proj.bias)
+            y.square().sum().backward()
+            return time.perf_counter() - t
+        m = self._module(ref)
+        t = time.perf_counter()
+        m(x).square().sum().backward()
+        return time.perf_counter() - t
+
+    def cpu_units(self, sample):
+        return self.units(sample)
+
+
+class Cfg5(Workload):
+    unit = "tokens/s"
+    batch = 64
+    shape = (4, 19, 30, 200)
+
+    def __init__(self, channel_mix):
+        self.channel_mix = channel_mix
+        self.key = "cfg5c" if channel_mix else "cfg5"
+        self.name = ("cfg5: Morlet" + ("ChannelMix" if channel_mix else "") + "Attention, 19 "
+                     "channels, hidden 200, x float32 (64, 4, 19, 30, 200), forward + backward "
+                     "of sum(y^2)")
+
+    def units(self, batch):  # tokens = B * C * T patches
+        return batch * 19 * 30
+
+    def _module(self, F):
+        import torch
+        torch.manual_seed(0)
+        cls = F.MorletChannelMixAttention if self.channel_mix else F.MorletAttention
+        return cls(num_channels=19, hidden_dim=200)
+
+    def setup(self, dev, batch):
+        import torch
+        import pytorch_morlet_fdwt_b200 as F
+        m = self._module(F).to(dev)
+        return {"m": m, "x": torch.randn((batch,) + self.shape, device=dev).requires_grad_()}
+
+    fwd = Cfg4.fwd
+    bwd = Cfg4.bwd
+    e2e_step = Cfg4.e2e_step
+
+    def kernel(self, st):
+        import torch
+        from pytorch_morlet_fdwt_b200.cwt import _softmax_backward, _softmax_forward
+        m = st["m"]
+        x = st["x"].detach()
+        B = x.shape[0]
+        x2 = x.reshape(-1, 6000)
+        H = m.cwt._filters(x2.device, torch.float32).detach()
+        if self.channel_mix:
+            v = x.reshape(B, 4, 19, 6000)
+            V = torch.einsum("fk,bhkn->bhfn", m.freq_to_channel.detach(), v).reshape(B * 4, 16,
+                                                                                      6000)
+        else:
+            V = m.freq_weight.detach()
+        out, mm, ll = _softmax_forward(x2, m.cwt.plan, H, V, 19, m.temperature)
+        g = torch.randn_like(out)
+        fma = 3 * _fma_per_position(m.cwt.plan) * x2.numel()
+        return ("cwt_backward_kernel<float,2> + reduce_rows_kernel (spectral softmax backward: "
+                "recompute, adjoint, filter gradient)",
+                lambda: _softmax_backward(g, x2, m.cwt.plan, H, V, 19, m.temperature, mm, ll, out,
+                                          True, True), fma, "fma")
+
+    def cpu(self, ref, sample):
+        import torch
+        x = torch.randn((sample,) + self.shape, requires_grad=True)
+        if ref is None:
+            import pytorch_morlet_fdwt_b200 as F
+            from oracle import cwt_oracle as C
+            m = self._module(F).double()
+            po = C.Plan(m.cwt.plan.scales, support_margin=1.25)
+            ls = m.cwt.log_scales.detach().double().requires_grad_()
+            w0 = torch.tensor(m.cwt.w0_value, dtype=torch.float64, requires_grad=True)
+            xd = x.detach().double().requires_grad_()
+            t = time.perf_counter()
+            H = po.filters(ls.exp(), w0)
+            if self.channel_mix:
+                y = C.channel_mix_attention(xd, po, H, m.freq_to_channel, m.temperature)
+            else:
+                y = C.attention(xd, po, H, m.freq_weight, m.temperature)
+            y.square().sum().backward()
+            return time.perf_counter() - t
+        m = self._module(ref)
+        t = time.perf_counter()
+        m(x).square().sum().backward()
+        return time.perf_counter() - t
+
+    def cpu_units(self, sample):
+        return self.units(sample)
+
+
+WORKLOADS = {"cfg1": Cfg1(), "cfg2": Cfg2(), "cfg3": Cfg3(False), "cfg3l": Cfg3(True),
+             "cfg4": Cfg4(), "cfg5": Cfg5(False), "cfg5c": Cfg5(True)}
+
+
+def cpu_baseline(W, reps=3):
+    """The reference's CPU path (or the port) on the workload's bounded sample, all host
+    threads; returns the cpu_baseline object."""
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ref = reference_package()
+    kind = "reference" if ref is not None else "port"
+    sample = W.cpu_sample
+    t, _ = cpu_time(lambda: W.cpu(ref, sample), reps)
+    units = W.cpu_units(sample)
+    scale = 1e9 if W.unit == "GB/s" else 1.0
+    what = ("the reference package's CPU PyTorch path (fdwt from baseline/_ref, CPU tensors)"
+            if ref is not None else "the fp64 CPU oracle port of the reference's CPU path")
+    return {"value": round(units / t / scale, 4), "unit": W.unit, "cores": threads,
+            "kind": kind, "cpu": cpu_model(),
+            "sample": f"{sample} {W.cpu_sample_unit} of the workload per step through {what}, "
+                      f"{threads} threads, median of {reps} after 1 warm-up ({t:.3f} s each)"}
+
+
+# ------------------------------------------------------------------------------ GPU timing
+
+def time_steps(W, st, steps, warmup, world, dev, barrier):
+    """Device time (ms) of `steps` fwd+bwd steps, and the mean fwd / bwd call times; max over
+    ranks.  Also the launches of this library inside the timed region."""
+    import torch
+    from pytorch_morlet_fdwt_b200 import _lib
+    for _ in range(warmup):
+        W.fwd(st)
+        W.bwd(st)
     torch.cuda.synchronize()
-
-    # device time of the two multilevel calls of the step (wavedec; also the waverec backward,
-    # and waverec; also the wavedec backward), each timed on its forward call
-    ka, kb, kc = ([torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-                  for _ in range(3))
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = _lib.launch_count()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        start.record()
-        for i in range(args.steps):
-            x.grad = None
-            ka[i].record()
-            coeffs = F.wavedec(x, bank, mode, level)
-            kb[i].record()
-            y = F.waverec(coeffs, bank, mode)
-            kc[i].record()
-            torch.autograd.backward(y, gy)
-        end.record()
-        torch.cuda.synchronize()
+    l0 = _lib.launch_count()
+    for e in ev:
+        e[0].record()
+        W.fwd(st)
+        e[1].record()
+        W.bwd(st)
+        e[2].record()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - l0
     barrier()
-    launches = _lib.launch_count() - launches0
-    ms = start.elapsed_time(end)
-    ana_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ka, kb))
-    syn_ms = statistics.mean(b.elapsed_time(c) for b, c in zip(kb, kc))
-    ms, ana_ms, syn_ms = max_over_ranks([ms, ana_ms, syn_ms], world, dev)
-    kernels = finest_launch_ms(F, _lib, x0, bank, mode, max(3, args.steps), barrier)
-    vals = max_over_ranks(list(kernels.values()), world, dev)
-    kernels = dict(zip(kernels, vals))
+    ms = ev[0][0].elapsed_time(ev[-1][2])
+    fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    ms, fwd, bwd = max_over_ranks([ms, fwd, bwd], world, dev)
+    return ms, fwd, bwd, launches
 
-    # end to end through the public API with host buffers (pinned), every step
-    e2e_steps = max(1, min(args.steps, 10))
-    e2e_ms = float("nan")
-    if args.no_e2e:
-        return _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms,
-                            kernels, launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
-    e2e_ms = e2e_pipelined(step, x0, e2e_steps, max(1, args.warmup // 2), barrier)
-    (e2e_ms,) = max_over_ranks([e2e_ms], world, dev)
-    return _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms,
-                        kernels, launches, clk, pool, x0, e2e_steps, e2e_ms, shape)
+
+def time_call(fn, reps, barrier):
+    """Mean device time (ms) of one call of fn over `reps` back-to-back calls, and the number of
+    this library's launches per call."""
+    import torch
+    from pytorch_morlet_fdwt_b200 import _lib
+    for _ in range(2):
+        fn()
+    barrier()
+    torch.cuda.synchronize()
+    l0 = _lib.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps, (_lib.launch_count() - l0) / reps
 
 
 def e2e_pipelined(step, x0, steps, warmup, barrier):
     """Device time of `steps` end-to-end steps: every step copies its input from pinned host
-    memory (host->device), runs the step through the public API and copies the result (the
-    input gradient, as large as the input) back to pinned host memory.  The copies run on
-    their own streams, double-buffered, so that step i+1's upload and step i's download overlap
-    step i's kernels and each other (PCIe is full duplex); the timed region runs from the first
-    upload to the last download."""
+    memory (host->device), runs the step through the public API and copies the step's result
+    (`step` returns it) back to pinned host memory.  The copies run on their own streams,
+    double-buffered, so that step i+1's upload and step i's download overlap step i's kernels
+    and each other (PCIe is full duplex); the timed region runs from the first upload to the
+    last download.  Returns (ms, d2h bytes per step)."""
     import torch
     dev = x0.device
-    xh = x0.cpu().pin_memory()
-    gh = [torch.empty_like(xh).pin_memory() for _ in range(2)]
-    xd = [torch.empty_like(x0) for _ in range(2)]
+    xh = x0.detach().cpu().pin_memory()
+    xd = [torch.empty_like(x0, requires_grad=False) for _ in range(2)]
+    with torch.no_grad():
+        xd[0].copy_(x0)
+    probe = step(xd[0].detach().requires_grad_(x0.requires_grad))
+    gh = [torch.empty(probe.shape, dtype=probe.dtype).pin_memory() for _ in range(2)]
+    d2h = probe.numel() * probe.element_size()
+    del probe
     comp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev = lambda: torch.cuda.Event(enable_timing=False)
+    ev = lambda: torch.cuda.Event(enable_timing=False)  # noqa: E731
 
     def run(n, timed):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         uploaded = [ev() for _ in range(n)]
         consumed = [None, None]   # compute done with xd[b]
         computed = [ev() for _ in range(n)]
-        downloaded = [None, None]  # gh[b] and the gradient of the step that used b are free
-        grads = [None, None]
+        downloaded = [None, None]  # gh[b] and the result of the step that used b are free
+        results = [None, None]
         if timed:
             start.record(s_in)
         for i in range(n):
@@ -316,15 +783,14 @@ def e2e_pipelined(step, x0, steps, warmup, barrier):
             comp.wait_event(uploaded[i])
             if downloaded[b] is not None:
                 comp.wait_event(downloaded[b])
-            xe = xd[b].detach().requires_grad_()
-            step(xe)
-            grads[b] = xe.grad
+            xe = xd[b].detach().requires_grad_(x0.requires_grad)
+            results[b] = step(xe)
             consumed[b] = ev()
             consumed[b].record(comp)
             computed[i].record(comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(computed[i])
-                gh[b].copy_(grads[b], non_blocking=True)
+                gh[b].copy_(results[b], non_blocking=True)
                 downloaded[b] = ev()
                 downloaded[b].record(s_out)
         if timed:
@@ -335,50 +801,142 @@ def e2e_pipelined(step, x0, steps, warmup, barrier):
     run(warmup, False)
     barrier()
     torch.cuda.synchronize()
-    return run(steps, True)
+    return run(steps, True), d2h
 
 
-def finest_launch_ms(F, _lib, x0, bank, mode, reps, barrier):
-    """Device time of one launch of each dominant kernel: the two finest levels of the analysis
-    (a two-level wavedec of the whole batch: one dwt_ana2_stream_kernel launch) and of the
-    synthesis (a two-level waverec: one dwt_syn2_stream_kernel launch), each the largest launch
-    of its direction in the step.  Timed with CUDA events around `reps` back-to-back calls
-    (each call must be one launch)."""
+# ------------------------------------------------------------------------------ our arm
+
+def measure_config(W, args, world, dev, barrier, cpu, fp32_peak, batch=None, full=True):
+    """One config's object: value, timing, roofline, e2e (and the given cpu baseline)."""
     import torch
-    x2 = x0.reshape(-1, x0.shape[-1])
-    c2 = F.wavedec(x2, bank, mode, 2)
-    out = {}
-    for name, fn in (("dwt_ana2_stream_kernel<float,16>", lambda: F.wavedec(x2, bank, mode, 2)),
-                     ("dwt_syn2_stream_kernel<float,16,0>", lambda: F.waverec(c2, bank, mode))):
-        for _ in range(2):
-            fn()
-        barrier()
-        torch.cuda.synchronize()
-        l0 = _lib.launch_count()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        if _lib.launch_count() - l0 != reps:
-            raise RuntimeError(f"{name}: a two-level call was not exactly one launch")
-        out[name] = e0.elapsed_time(e1) / reps
+    batch = W.batch if batch is None else batch
+    torch.manual_seed(100 + (dev.index or 0))
+    st = W.setup(dev, batch)
+    steps = args.steps
+    ms, fwd, bwd, launches = time_steps(W, st, steps, max(3, args.warmup), world, dev, barrier)
+    units = W.units(batch)
+    scale = 1e9 if W.unit == "GB/s" else 1.0
+    out = {"workload": W.name + ("" if batch == W.batch else f" [batch {batch} per GPU]"),
+           "value": round(job_throughput(units, steps, world, ms, scale), 3), "unit": W.unit,
+           "ms_per_step": round(ms / steps, 4), "fwd_ms": round(fwd, 4),
+           "bwd_ms": round(bwd, 4), "gpu_launches": int(launches),
+           "units_per_step_per_gpu": units}
+    if not full:
+        return out
+    name, fn, work, bound = W.kernel(st)
+    k_ms, per_call = time_call(fn, max(3, steps), barrier)
+    (k_ms,) = max_over_ranks([k_ms], world, dev)
+    if bound == "hbm":
+        peak, src = peaks()
+        achieved = work / (k_ms / 1e3) / 1e9
+        out["roofline"] = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1),
+                           "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                           "peak_source": src, "algorithmic_bytes_per_call": work,
+                           "call_ms": round(k_ms, 4), "launches_per_call": per_call,
+                           "traffic": None}
+    else:
+        achieved = 2 * work / (k_ms / 1e3) / 1e12
+        out["roofline"] = {"bound": "fp32 fma", "kernel": name, "achieved": round(achieved, 2),
+                           "peak": round(fp32_peak / 1e3, 2), "unit": "TFLOP/s",
+                           "frac": round(achieved * 1e3 / fp32_peak, 4),
+                           "peak_source": "measured in this run: cuBLAS SGEMM 8192^3, TF32 off",
+                           "algorithmic_fma_per_call": work,
+                           "fma_count": "3 forward filter-bank passes (recompute W, adjoint, "
+                                        "filter gradient), each sum over scales of (2 * "
+                                        "half-support + 1) FMAs per position after folding",
+                           "call_ms": round(k_ms, 4), "launches_per_call": per_call,
+                           "traffic": None}
+    if not args.no_e2e:
+        n_e2e = max(2, min(steps, 5))
+        e_ms, d2h = e2e_pipelined(lambda x: W.e2e_step(st, x), st["x"], n_e2e, 2, barrier)
+        (e_ms,) = max_over_ranks([e_ms], world, dev)
+        x = st["x"]
+        out["e2e"] = {"value": round(job_throughput(units, n_e2e, world, e_ms, scale), 3),
+                      "unit": W.unit, "h2d_bytes_per_step": x.numel() * x.element_size(),
+                      "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms / n_e2e, 3)}
+    if cpu is not None:
+        out["cpu_baseline"] = cpu
+    del st
+    torch.cuda.empty_cache()
     return out
 
 
-def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, syn_ms, kernels,
-                 launches, clk, pool, x0, e2e_steps, e2e_ms, shape):
+def run_headline(args, rank, world, local_rank, cpu):
+    import torch
+    import torch.distributed as dist
+    from pytorch_morlet_fdwt_b200 import _lib
+    dev = torch.device("cuda", local_rank)
+    W = WORKLOADS["cfg2"]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    torch.manual_seed(1234 + rank)
+    st = W.setup(dev, W.batch, rows=args.rows)
+    R = st["x"].numel() // W.shape[-1]
+    step_bytes = 4 * W.dir_bytes_per_row() * R
+    for _ in range(args.warmup):
+        W.fwd(st)
+        W.bwd(st)
+    torch.cuda.synchronize()
+    ka, kb, kc = ([torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+                  for _ in range(3))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    F, bank = st["F"], st["bank"]
+    with ClockSampler(local_rank) as clk:
+        start.record()
+        for i in range(args.steps):
+            st["x"].grad = None
+            ka[i].record()
+            coeffs = F.wavedec(st["x"], bank, W.mode, W.level)
+            kb[i].record()
+            y = F.waverec(coeffs, bank, W.mode)
+            kc[i].record()
+            torch.autograd.backward(y, st["gy"])
+        end.record()
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    barrier()
+    ms = start.elapsed_time(end)
+    ana_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ka, kb))
+    syn_ms = statistics.mean(b.elapsed_time(c) for b, c in zip(kb, kc))
+    ms, ana_ms, syn_ms = max_over_ranks([ms, ana_ms, syn_ms], world, dev)
+    kern = {}
+    for name, fn in W.kernels(st).items():
+        k_ms, per_call = time_call(fn, max(3, args.steps), barrier)
+        if per_call != 1:
+            raise RuntimeError(f"{name}: a two-level call was not exactly one launch")
+        kern[name] = k_ms
+    vals = max_over_ranks(list(kern.values()), world, dev)
+    kern = dict(zip(kern, vals))
+    e2e = None
+    if not args.no_e2e:
+        n_e2e = max(1, min(args.steps, 10))
+        e_ms, d2h = e2e_pipelined(lambda x: W.e2e_step(st, x), st["x"], n_e2e,
+                                  max(1, args.warmup // 2), barrier)
+        (e_ms,) = max_over_ranks([e_ms], world, dev)
+        e2e = {"value": round(step_bytes * n_e2e * world / (e_ms / 1e3) / 1e9, 2),
+               "unit": "GB/s", "h2d_bytes_per_step": st["x"].numel() * 4,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms / n_e2e, 3),
+               "copies": "input upload and gradient download of every step on their own "
+                         "streams, double-buffered: step i+1's upload and step i's download "
+                         "overlap step i's kernels"}
+    x_shape = tuple(st["x"].shape)
+    del st
+    torch.cuda.empty_cache()
     if rank != 0:
         return None
     peak, peak_src = peaks()
-    value = job_throughput(step_bytes, args.steps, world, ms, 1e9)
-    dominant = max(kernels, key=kernels.get)
-    kern_ms = kernels[dominant]
-    achieved = dir_bytes_row * R / (kern_ms / 1e3) / 1e9
+    dominant = max(kern, key=kern.get)
+    kern_ms = kern[dominant]
+    achieved = W.dir_bytes_per_row() * R / (kern_ms / 1e3) / 1e9
     line = {
         "metric": METRIC,
-        "value": round(value, 2),
+        "value": round(job_throughput(step_bytes, args.steps, world, ms, 1e9), 2),
         "unit": "GB/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -390,8 +948,8 @@ def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, sy
         "dtype": "f32",
         "data": "synthetic i.i.d. N(0,1), seeded per rank",
         "config": {
-            "workload": "cfg2: db8 periodization level-8 wavedec + waverec + backward through "
-                        f"both, x float32 {tuple(shape)} per GPU",
+            "workload": W.name + f" per GPU",
+            "shape_per_gpu": x_shape,
             "algorithmic_bytes_per_step": step_bytes,
             "l2": "inputs larger than L2 (512 MiB per array)",
             "parallelism": f"rows sharded by rank, {world} GPU(s), no collective",
@@ -400,287 +958,77 @@ def _finish_cfg2(args, rank, world, R, step_bytes, dir_bytes_row, ms, ana_ms, sy
             "bound": "hbm", "kernel": dominant,
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_src,
-            "algorithmic_bytes_per_launch": dir_bytes_row * R,
+            "algorithmic_bytes_per_launch": W.dir_bytes_per_row() * R,
             "launch_ms": round(kern_ms, 4),
             "traffic": TRAFFIC_PER_LAUNCH.get(dominant),
-            "kernels_ms_per_launch": {k: round(v, 4) for k, v in kernels.items()},
+            "kernels_ms_per_launch": {k: round(v, 4) for k, v in kern.items()},
             "launch": "the two finest levels of the step's analysis / synthesis in one launch "
                       "over every row: x (or the level-1 details and level-2 coefficients) "
                       "read once, the other side written once",
-            "calls_ms": {"wavedec (8 levels, 4 launches)": round(ana_ms, 4),
-                         "waverec (8 levels, 4 launches)": round(syn_ms, 4)},
+            "calls_ms": {"wavedec (8 levels)": round(ana_ms, 4),
+                         "waverec (8 levels)": round(syn_ms, 4)},
         },
         "gpu_launches": int(launches),
-        "e2e": None if args.no_e2e else {
-            "value": round(step_bytes * e2e_steps * world / (e2e_ms / 1e3) / 1e9, 2),
-            "unit": "GB/s",
-            "h2d_bytes_per_step": x0.numel() * 4,
-            "d2h_bytes_per_step": x0.numel() * 4,
-            "ms_per_step": round(e2e_ms / e2e_steps, 3),
-            "copies": "input upload and gradient download of every step on their own streams, "
-                      "double-buffered: step i+1's upload and step i's download overlap step "
-                      "i's kernels",
-        },
+        "e2e": e2e,
         "clocks": clk.summary(),
     }
-    if pool is not None:
-        gbs, t, rows = cpu_sample(pool, rows=args.cpu_rows, reps=3)
-        line["cpu_baseline"] = {
-            "value": round(gbs, 3), "unit": "GB/s", "cores": pool.cores, "kind": "port",
-            "sample": f"{rows} of the 2048 rows of the cfg2 step (wavedec, waverec, both "
-                      f"vjps) with the oracle's sparse-operator restatement in fp32, median of 3 "
-                      f"({t:.2f} s each)",
-        }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
     return line
 
 
-# ------------------------------------------------------------------------------ reference arm
-
-def run_reference(args, pool):
-    times = []
-    rows_done = 0
-    for i in range(args.warmup + args.steps):
-        t, rows_done = pool.step(args.cpu_rows)
-        if i >= args.warmup:
-            times.append(t)
-    step_bytes_row, _ = cfg2_bytes_per_row()
-    t = statistics.mean(times)
-    value = step_bytes_row * rows_done / t / 1e9
-    sample = (f"{rows_done} rows of the cfg2 step per step (wavedec, waverec, both vjps) with the "
-              f"oracle port of the reference's CPU path, fp32, {pool.cores} worker processes")
-    return {
-        "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t * 1e3, 2), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1)",
-        "config": {"workload": "cfg2: db8 periodization level-8 wavedec + waverec + backward "
-                               "through both (bounded row sample of (16,128,65536))"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": pool.cores,
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-
-
-# ------------------------------------------------------------------------------ other configs
-#
-# The other baseline configs (2, 3, 4), measured the same way on demand with
-# --config; each prints its own line.  The forward and the backward calls are timed separately
-# with CUDA events; the kernel named in "roofline" is the one with the larger share.
-
-
-def _cfg_cwt_plan(learnable):
-    import pytorch_morlet_fdwt_b200 as F
-    return F.CWT1D(freqs=np.logspace(-0.3, 2, 40), fs=250.0, norm="l1", learnable=learnable,
-                   learnable_w0=learnable)
-
-
-def _wl_cfg1():
-    import torch
-    import pytorch_morlet_fdwt_b200 as F
-    from oracle.dwt_oracle import dwt_coeff_len
-    n, lv = 2500, 5
-    lens, cur = [], n
-    for _ in range(lv):
-        cur = dwt_coeff_len(cur, 8, "symmetric")
-        lens.append(cur)
-    rows = 32 * 64
-    per_dir = rows * (n + sum(lens) + lens[-1]) * 4
-
-    def setup(dev):
-        return {"x": torch.randn(32, 64, n, device=dev).requires_grad_(),
-                "bank": F.get_filter_bank("db4")}
-
-    def fwd(st):
-        st["c"] = F.wavedec(st["x"], st["bank"], "symmetric", lv)
-        st["y"] = F.waverec([c.detach() for c in st["c"]], st["bank"], "symmetric")
-
-    def bwd(st):
-        st["x"].grad = None
-        sum((c * c).sum() for c in st["c"]).backward()
-
-    def cpu(rows_s):
-        from oracle import dwt_oracle as D
-        b = F.get_filter_bank("db4")
-        tb = (b.dec_lo, b.dec_hi, b.rec_lo, b.rec_hi)
-        x = np.random.default_rng(0).standard_normal((rows_s, n)).astype(np.float32)
-        t = time.perf_counter()
-        c = D.wavedec(x, tb, "symmetric", lv)
-        D.waverec(c, tb, "symmetric")
-        D.wavedec_vjp(n, [2 * v for v in c], tb, "symmetric")
-        return time.perf_counter() - t
-
-    return dict(name="cfg1: db4 symmetric level-5 wavedec, waverec and the backward of "
-                     "sum(coeffs^2), x float32 (32,64,2500)",
-                unit="GB/s", per_step=3 * per_dir, rows=rows, setup=setup, fwd=fwd, bwd=bwd,
-                cpu=cpu, cpu_rows=2048, dtype="f32",
-                kernels=("dwt_analysis_kernel + dwt_syn_tile_kernel (waverec)",
-                         "dwt_syn_tile_kernel (backward)"),
-                fwd_bytes=2 * per_dir, bwd_bytes=per_dir)
-
-
-def _wl_cfg3(learnable, rows=None):
-    import torch
-    from oracle import cwt_oracle as C
-    shape = (32 if rows is None else max(1, rows // 64), 64, 2500)
-    rows = shape[0] * shape[1]
-    x_bytes = rows * 2500 * 4
-    w_bytes = rows * 40 * 2500 * 8
-
-    def setup(dev):
-        m = _cfg_cwt_plan(learnable).to(dev)
-        return {"m": m, "x": torch.randn(shape, device=dev).requires_grad_(learnable)}
-
-    def fwd(st):
-        st["y"] = st["m"](st["x"])
-
-    def bwd(st):
-        if learnable:
-            st["x"].grad = None
-            st["m"].zero_grad()
-            torch.view_as_real(st["y"]).square().sum().backward()
-
-    def cpu(rows_s):
-        m = _cfg_cwt_plan(learnable)
-        po = C.Plan(m.plan.scales, norm="l1", support_margin=1.25 if learnable else 1.0)
-        ls = torch.tensor(m.plan.scales, dtype=torch.float64).log().requires_grad_(learnable)
-        w0 = torch.tensor(6.0, dtype=torch.float64, requires_grad=learnable)
-        x = torch.randn(rows_s, 2500, dtype=torch.float64, requires_grad=learnable)
-        t = time.perf_counter()
-        W = C.apply_plan(x, po, po.filters(ls.exp(), w0))
-        if learnable:
-            W.abs().square().sum().backward()
-        return time.perf_counter() - t
-
-    fb = x_bytes + w_bytes
-    bb = w_bytes + 2 * x_bytes if learnable else 0
-    name = ("cfg3: Morlet CWT fast, 40 freqs logspace(-0.3,2) @ 250 Hz, l1, x float32 "
-            f"{shape} -> complex64 ({shape[0]},64,40,2500)")
-    if learnable:
-        name += "; learnable scales and w0, backward of sum |W|^2"
-    return dict(name=name, unit="GB/s", per_step=fb + bb, rows=rows, setup=setup, fwd=fwd,
-                bwd=bwd, cpu=cpu, cpu_rows=32 if learnable else 64, dtype="f32",
-                kernels=("cwt_forward_kernel<float,float,0>", "cwt_backward_kernel<float,0>"),
-                fwd_bytes=fb, bwd_bytes=bb)
-
-
-def _wl_cfg4():
-    import torch
-    import pytorch_morlet_fdwt_b200 as F
-    from oracle import cwt_oracle as C
-    freqs = np.logspace(0, 1.8, 16).tolist()
-
-    def setup(dev):
-        torch.manual_seed(0)
-        m = F.MorletTokenMixer(256, freqs=freqs, fs=250).to(dev)
-        return {"m": m, "x": torch.randn(8, 4096, 256, device=dev).requires_grad_()}
-
-    def fwd(st):
-        st["y"] = st["m"](st["x"])
-
-    def bwd(st):
-        st["x"].grad = None
-        st["m"].zero_grad()
-        st["y"].square().sum().backward()
-
-    def cpu(batch):
-        torch.manual_seed(0)
-        m = F.MorletTokenMixer(256, freqs=freqs, fs=250).double()
-        po = C.Plan(m.cwt.plan.scales, support_margin=1.25)
-        x = torch.randn(batch, 4096, 256, dtype=torch.float64, requires_grad=True)
-        ls = m.cwt.log_scales.detach().double().requires_grad_()
-        t = time.perf_counter()
-        y = C.token_mixer(x, po, po.filters(ls.exp(), m.cwt.w0_value), m.mag_weight,
-                          m.phase_weight, m.bias, m.out_proj.weight, m.out_proj.bias)
-        y.square().sum().backward()
-        return time.perf_counter() - t
-
-    return dict(name="cfg4: MorletTokenMixer dim 256, 16 freqs logspace(0,1.8) @ 250 Hz, "
-                     "x float32 (8,4096,256), forward + backward",
-                unit="tokens/s", per_step=8 * 4096, rows=8 * 256, setup=setup, fwd=fwd, bwd=bwd,
-                cpu=cpu, cpu_rows=1, cpu_unit_per_row=4096, cpu_reps=1, dtype="f32",
-                kernels=("cwt_forward_kernel<float,float,1> (mix)",
-                         "cwt_backward_kernel<float,1> (mix)"),
-                fwd_bytes=2 * 8 * 4096 * 256 * 4, bwd_bytes=3 * 8 * 4096 * 256 * 4)
-
-
-def _wl_cfg5(channel_mix):
-    import torch
-    import pytorch_morlet_fdwt_b200 as F
-    from oracle import cwt_oracle as C
-    cls = F.MorletChannelMixAttention if channel_mix else F.MorletAttention
-
-    def setup(dev):
-        torch.manual_seed(0)
-        m = cls(num_channels=19, hidden_dim=200).to(dev)
-        return {"m": m, "x": torch.randn(64, 4, 19, 30, 200, device=dev).requires_grad_()}
-
-    def fwd(st):
-        st["y"] = st["m"](st["x"])
-
-    def bwd(st):
-        st["x"].grad = None
-        st["m"].zero_grad()
-        st["y"].square().sum().backward()
-
-    def cpu(batch):
-        torch.manual_seed(0)
-        m = cls(num_channels=19, hidden_dim=200).double()
-        po = C.Plan(m.cwt.plan.scales, support_margin=1.25)
-        x = torch.randn(batch, 4, 19, 30, 200, dtype=torch.float64, requires_grad=True)
-        ls = m.cwt.log_scales.detach().double().requires_grad_()
-        w0 = torch.tensor(m.cwt.w0_value, dtype=torch.float64, requires_grad=True)
-        H = po.filters(ls.exp(), w0)
-        t = time.perf_counter()
-        if channel_mix:
-            y = C.channel_mix_attention(x, po, H, m.freq_to_channel, m.temperature)
-        else:
-            y = C.attention(x, po, H, m.freq_weight, m.temperature)
-        y.square().sum().backward()
-        return time.perf_counter() - t
-
-    name = ("cfg5: Morlet" + ("ChannelMix" if channel_mix else "") + "Attention, 19 channels, "
-            "hidden 200, x float32 (64,4,19,30,200), forward + backward")
-    return dict(name=name, unit="tokens/s", per_step=64 * 19 * 30, rows=64 * 4 * 19,
-                setup=setup, fwd=fwd, bwd=bwd, cpu=cpu, cpu_rows=1, cpu_unit_per_row=19 * 30,
-                dtype="f32",
-                kernels=("cwt_forward_kernel<float,float,2> (spectral softmax)",
-                         "cwt_backward_kernel<float,2> (spectral softmax)"),
-                fwd_bytes=2 * 64 * 4 * 19 * 6000 * 4, bwd_bytes=3 * 64 * 4 * 19 * 6000 * 4)
-
-
-WORKLOADS = {
-    "cfg1": _wl_cfg1,
-    "cfg3": lambda rows=None: _wl_cfg3(False, rows),
-    "cfg3l": lambda rows=None: _wl_cfg3(True, rows),
-    "cfg4": _wl_cfg4,
-    "cfg5": lambda: _wl_cfg5(False),
-    "cfg5c": lambda: _wl_cfg5(True),
-}
-
-
-def run_config(args, rank, world, local_rank):
+def run_strong_and_gather(args, rank, world, local_rank):
+    """At N > 1: the headline config with its batch split over the ranks (strong scaling), and
+    the optional NCCL all-gather of the per-rank input gradients, timed apart."""
     import torch
     import torch.distributed as dist
-    from pytorch_morlet_fdwt_b200 import _lib
-    W = WORKLOADS[args.config](args.rows) if args.rows else WORKLOADS[args.config]()
-    # CPU baseline first (before any CUDA work), rank 0 at N=1
-    cpu_line = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        import torch as _t
-        _t.set_num_threads(os.cpu_count() or 1)
-        reps = W.get("cpu_reps", 3)
-        if reps > 1:
-            W["cpu"](W["cpu_rows"])  # warm-up
-        times = [W["cpu"](W["cpu_rows"]) for _ in range(reps)]
-        tc = statistics.median(times)
-        units = W.get("cpu_unit_per_row")
-        per = (W["cpu_rows"] * units) if units else W["per_step"] * W["cpu_rows"] / W["rows"]
-        cpu_line = {"value": round(per / tc / (1e9 if W["unit"] == "GB/s" else 1), 4),
-                    "unit": W["unit"], "cores": os.cpu_count(), "kind": "port",
-                    "sample": f"{W['cpu_rows']} {'batch entries' if units else 'rows'} of the "
-                              f"workload through the fp64 CPU oracle (torch, all cores), median "
-                              f"of {reps} ({tc:.2f} s each)"}
+    from pytorch_morlet_fdwt_b200.sharding import gather_batch, shard_bounds
+    dev = torch.device("cuda", local_rank)
+    W = WORKLOADS["cfg2"]
+    b0, b1 = shard_bounds(W.batch, rank, world)
+    res = {}
+    if b1 - b0 >= 1 and W.batch % world == 0:
+        m = measure_config(W, args, world, dev, dist.barrier, None, None, batch=b1 - b0,
+                           full=False)
+        m["scaling"] = "strong"
+        m["split"] = f"batch {W.batch} over {world} GPUs: {b1 - b0} per GPU"
+        res["strong_scaling"] = m
+        torch.manual_seed(7 + rank)
+        st = W.setup(dev, b1 - b0)
+        W.fwd(st)
+        W.bwd(st)
+        g = st["x"].grad
+        for _ in range(2):
+            gather_batch(g)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        reps = 5
+        for _ in range(reps):
+            out = gather_batch(g)
+        e1.record()
+        torch.cuda.synchronize()
+        (g_ms,) = max_over_ranks([e0.elapsed_time(e1) / reps], world, dev)
+        nbytes = out.numel() * out.element_size()
+        res["gather"] = {"what": "all_gather_into_tensor of every rank's dL/dx shard (NCCL), "
+                                 "outside the device-timed step",
+                         "bytes": nbytes, "ms": round(g_ms, 4),
+                         "algbw_gbs": round(nbytes / (g_ms / 1e3) / 1e9, 1)}
+        del st, out
+        torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    names = CONFIG_NAMES if args.config == "all" else (
+        [] if args.config == "cfg2" else [args.config])
+    headline = args.config in ("all", "cfg2")
+    # the CPU baselines (rank 0 at N=1) run after every GPU measurement: their host threads
+    # must not compete with the thread that launches the timed steps
+    cpu = {}
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local_rank)
@@ -688,93 +1036,97 @@ def run_config(args, rank, world, local_rank):
                                 device_id=torch.device("cuda", local_rank))
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    torch.manual_seed(100 + rank)
-    st = W["setup"](dev)
-    for _ in range(args.warmup):
-        W["fwd"](st)
-        W["bwd"](st)
-    torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    l0 = _lib.launch_count()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        for e in ev:
-            e[0].record()
-            W["fwd"](st)
-            e[1].record()
-            W["bwd"](st)
-            e[2].record()
-        torch.cuda.synchronize()
-    launches = _lib.launch_count() - l0
-    ms = ev[0][0].elapsed_time(ev[-1][2])
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
-    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
-    ms, fwd_ms, bwd_ms = max_over_ranks([ms, fwd_ms, bwd_ms], world, dev)
-    if world > 1:
-        dist.destroy_process_group()
-    if rank != 0:
-        return 0
-    scale = 1e9 if W["unit"] == "GB/s" else 1.0
-    value = job_throughput(W["per_step"], args.steps, world, ms, scale)
-    peak, peak_src = peaks()
-    dom = 0 if fwd_ms >= bwd_ms or W["bwd_bytes"] == 0 else 1
-    k_ms = fwd_ms if dom == 0 else bwd_ms
-    k_bytes = W["fwd_bytes"] if dom == 0 else W["bwd_bytes"]
-    achieved = k_bytes / (k_ms / 1e3) / 1e9
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": W["unit"], "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": W["dtype"],
-        "data": "synthetic i.i.d. N(0,1), random-init parameters, seeded",
-        "config": {"workload": W["name"], "l2": "outputs larger than L2" if W["unit"] == "GB/s"
-                   else "inputs and scalograms larger than L2 across a step"},
-        "roofline": {"bound": "hbm", "kernel": W["kernels"][dom], "achieved": round(achieved, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "peak_source": peak_src, "algorithmic_bytes_per_call": k_bytes,
-                     "call_ms": round(k_ms, 4), "traffic": None,
-                     "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4)},
-        "gpu_launches": int(launches),
-        "e2e": None,
-        "clocks": clk.summary(),
-    }
-    if cpu_line is not None:
-        line["cpu_baseline"] = cpu_line
-    print(json.dumps(line), flush=True)
+    barrier = dist.barrier if world > 1 else (lambda: None)
+    try:
+        line = run_headline(args, rank, world, local_rank, None) if headline else None
+        if world > 1 and headline and args.rows is None:
+            extra = run_strong_and_gather(args, rank, world, local_rank)
+            if line is not None:
+                line.update(extra)
+        fp32_peak = fp32_fma_peak(dev) if names else None
+        configs = {}
+        for k in names:
+            configs[k] = measure_config(WORKLOADS[k], args, world, dev, barrier, None, fp32_peak)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            torch.cuda.synchronize()
+            if line is not None:
+                line["cpu_baseline"] = cpu_baseline(WORKLOADS["cfg2"])
+            for k in names:
+                configs[k]["cpu_baseline"] = cpu_baseline(WORKLOADS[k])
+        if rank == 0:
+            if line is None:  # a single non-headline config: its object is the line
+                k = names[0]
+                c = configs[k]
+                line = {"metric": METRIC, "value": c["value"], "unit": c["unit"],
+                        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                        "ms_per_step": c["ms_per_step"], "higher_is_better": True,
+                        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                        "data": "synthetic i.i.d. N(0,1), random-init parameters, seeded",
+                        "config": {"workload": c["workload"]},
+                        "roofline": c.get("roofline"), "gpu_launches": c["gpu_launches"],
+                        "e2e": c.get("e2e")}
+                if "cpu_baseline" in c:
+                    line["cpu_baseline"] = c["cpu_baseline"]
+            elif configs:
+                line["configs"] = configs
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
     return 0
 
 
-def run_config_reference(args):
-    import torch
-    W = WORKLOADS[args.config]()
-    torch.set_num_threads(os.cpu_count() or 1)
-    times = []
-    steps, warmup = args.steps, args.warmup
-    for i in range(warmup + steps):
-        t = W["cpu"](W["cpu_rows"])
-        if i >= warmup:
-            times.append(t)
-        if t > 5.0:  # a heavy sample: keep the whole run within a few minutes
-            steps, warmup = min(steps, 2), min(warmup, i)
-            if len(times) >= steps:
-                break
-    tc = statistics.mean(times) if times else t
-    units = W.get("cpu_unit_per_row")
-    per = (W["cpu_rows"] * units) if units else W["per_step"] * W["cpu_rows"] / W["rows"]
-    value = per / tc / (1e9 if W["unit"] == "GB/s" else 1)
-    sample = (f"{W['cpu_rows']} {'batch entries' if units else 'rows'} per step through the fp64 "
-              f"CPU oracle port of the reference's CPU path (torch, {os.cpu_count()} threads)")
-    return {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": W["unit"],
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(tc * 1e3, 2), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64", "data": "synthetic i.i.d. N(0,1)",
-            "config": {"workload": W["name"] + " (bounded sample)"},
-            "cpu_baseline": {"value": round(value, 4), "unit": W["unit"],
-                             "cores": os.cpu_count(), "kind": "port", "sample": sample},
-            "e2e": {"value": round(value, 4), "unit": W["unit"], "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+# ------------------------------------------------------------------------------ reference arm
 
+def run_reference(args, rank, world):
+    """The reference's own CPU path, rank 0 only: the headline config's bounded sample per step
+    (all host threads), plus each other config's sample (1 warm-up + 2 steps) when --config
+    all."""
+    if rank != 0:
+        return 0
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ref = reference_package()
+    kind = "reference" if ref is not None else "port"
+    key = "cfg2" if args.config in ("all", "cfg2") else args.config
+    W = WORKLOADS[key]
+    times = []
+    for i in range(args.warmup + args.steps):
+        t = W.cpu(ref, W.cpu_sample)
+        if i >= args.warmup:
+            times.append(t)
+    t = statistics.mean(times)
+    scale = 1e9 if W.unit == "GB/s" else 1.0
+    value = W.cpu_units(W.cpu_sample) / t / scale
+    what = ("the reference package's CPU PyTorch path (fdwt from baseline/_ref, CPU tensors)"
+            if ref is not None else "the fp64 CPU oracle port of the reference's CPU path")
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": W.unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1), seeded",
+        "config": {"workload": W.name + (" per GPU" if key == "cfg2" else "")},
+        "cpu_baseline": {"value": round(value, 4), "unit": W.unit, "cores": threads,
+                         "kind": kind, "cpu": cpu_model(),
+                         "sample": f"{W.cpu_sample} {W.cpu_sample_unit} of the workload per "
+                                   f"step through {what}, {threads} threads"},
+        "e2e": {"value": round(value, 4), "unit": W.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    if args.config == "all":
+        line["configs"] = {}
+        for k in CONFIG_NAMES:
+            Wk = WORKLOADS[k]
+            tk, _ = cpu_time(lambda: Wk.cpu(ref, Wk.cpu_sample), 2)
+            sk = 1e9 if Wk.unit == "GB/s" else 1.0
+            line["configs"][k] = {
+                "workload": Wk.name, "value": round(Wk.cpu_units(Wk.cpu_sample) / tk / sk, 4),
+                "unit": Wk.unit, "kind": kind,
+                "sample": f"{Wk.cpu_sample} {Wk.cpu_sample_unit} per step, median of 2 after 1 "
+                          f"warm-up ({tk:.3f} s each)"}
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def main():
@@ -783,58 +1135,21 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=2048)
+    ap.add_argument("--config", default="all", choices=["all", "cfg2"] + CONFIG_NAMES,
+                    help="all (default: the cfg2 headline line with every other config under "
+                         "'configs'), or one config alone")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--rows", type=int, default=None,
-                    help="cfg2, cfg3, cfg3l: rows per GPU (default: the config's; fewer for "
-                         "profiling)")
-    ap.add_argument("--config", default="cfg2", choices=["cfg2"] + sorted(WORKLOADS),
-                    help="cfg2 (default, the headline line) or another baseline config")
+                    help="cfg2 only: rows per GPU (default: the config's; fewer for profiling)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-
-    if args.config != "cfg2":
-        if args.impl == "reference":
-            if rank == 0:
-                print(json.dumps(run_config_reference(args)), flush=True)
-            return 0
-        return run_config(args, rank, world, local_rank)
-
     if args.impl == "reference":
-        if rank != 0:
-            return 0
-        pool = CpuPool(os.cpu_count() or 1)
-        try:
-            print(json.dumps(run_reference(args, pool)), flush=True)
-        finally:
-            pool.close()
-        return 0
-
-    # CPU pool first (spawned before the first CUDA call), rank 0 at N=1 only
-    pool = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        pool = CpuPool(os.cpu_count() or 1)
-    import torch
-    import torch.distributed as dist
-    if world > 1:
-        from datetime import timedelta
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
-    try:
-        line = run_ours(args, rank, world, local_rank, pool)
-        if line is not None:
-            print(json.dumps(line), flush=True)
-    finally:
-        if pool is not None:
-            pool.close()
-        if world > 1:
-            dist.destroy_process_group()
-    return 0
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local_rank)
 
 
 if __name__ == "__main__":

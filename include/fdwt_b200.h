@@ -64,6 +64,16 @@ void fdwt_set_shared_memory_fill(int enable, unsigned int word);
  * and return without finishing their work.  Synchronises the device, writes the code to
  * *code (0: none since the last call) and clears it. */
 int fdwt_device_error(int* code);
+/* Test hook of the bounded copy waits above (no counterpart in the reference).  While
+ * extra_tx_bytes > 0, the streaming DWT kernels expect that many bytes more than they copy for
+ * global tile 0, so its wait runs out without any fault (every issued copy still lands); the
+ * kernel then stores 1 in the error word, waits for its copies still in flight and returns.
+ * `tries` replaces the poll limit of the main waits (<= 0: the default 2^22); the wait for
+ * copies in flight after a timeout polls at least 2^20 times.  Process-wide; (0, 0) restores
+ * the defaults.  The per-device caches of this library (error word, device attributes,
+ * allocation-free scratch) assume each device's primary context lives as long as the process
+ * (no cudaDeviceReset between calls). */
+void fdwt_set_copy_wait_test(unsigned int extra_tx_bytes, long long tries);
 
 /* ------------------------------------------------------------------------------------------
  * Discrete wavelet transform.  One call runs every level of a multilevel transform (the

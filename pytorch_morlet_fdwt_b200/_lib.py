@@ -30,6 +30,10 @@ SIGNATURES = {
     "fdwt_launch_count": (ctypes.c_ulonglong, []),
     "fdwt_set_shared_memory_fill": (None, [ctypes.c_int, ctypes.c_uint]),
     "fdwt_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "fdwt_set_copy_wait_test": (None, [ctypes.c_uint, ctypes.c_longlong]),
+    "fdwt_dwt_analysis_noalloc": (ctypes.c_int, [
+        ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, c_i64p, c_i64p,
+        c_voidpp, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "fdwt_dwt_analysis": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, c_i64p, c_i64p,
         c_voidpp, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -168,6 +172,22 @@ def device_error() -> int:
     v = ctypes.c_int(0)
     check(load().fdwt_device_error(ctypes.byref(v)), "fdwt_device_error")
     return int(v.value)
+
+
+def check_device_error(what: str) -> None:
+    """Raise if a kernel gave up waiting on a copy since the last check (synchronises the
+    device).  Called after every DWT call while ``config.check_device_errors`` is set."""
+    code = device_error()
+    if code != 0:
+        raise RuntimeError(
+            f"{what}: a streaming kernel's bounded wait on an asynchronous copy ran out (device "
+            f"error {code}); its outputs are incomplete")
+
+
+def set_copy_wait_test(extra_tx_bytes: int, tries: int = 0) -> None:
+    """Test hook: make the bounded copy wait of global tile 0 run out (see
+    fdwt_set_copy_wait_test); ``(0, 0)`` restores the defaults."""
+    load().fdwt_set_copy_wait_test(int(extra_tx_bytes), int(tries))
 
 
 def set_shared_memory_fill(enable: bool, word: int = 0) -> None:

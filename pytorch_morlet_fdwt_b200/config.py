@@ -1,10 +1,17 @@
-"""Global precision switches (same names and defaults as the reference's ``fdwt/config.py:17-18``).
+"""Global switches (``allow_tf32`` / ``allow_bf16`` have the names and defaults of the
+reference's ``fdwt/config.py:17-18``).
 
-``allow_tf32`` and ``allow_bf16`` are read at call time.  The sm_100a kernels of this package
+``allow_tf32`` and ``allow_bf16`` are accepted for drop-in compatibility; the sm_100a kernels
 compute every filter-bank contraction with fp32 FMAs for fp32/fp16/bf16 inputs and fp64 FMAs
-for fp64 inputs, so both switches are accepted for drop-in compatibility and currently select
-the same full-precision kernels (results are at least as accurate as the reference's modes).
+for fp64 inputs whatever they say (results at least as accurate as the reference's modes).
+
+``check_device_errors`` (no counterpart in the reference) makes every DWT call synchronise and
+read the device error word afterwards, raising ``RuntimeError`` if a streaming kernel gave up
+waiting on an asynchronous copy (its outputs are then incomplete).  Off by default: the check
+costs a device synchronisation per call.  Without it, callers that need the guarantee poll
+``fdwt_device_error()`` (``_lib.device_error()``) themselves.
 """
 
 allow_tf32: bool = False
 allow_bf16: bool = False
+check_device_errors: bool = False

@@ -136,10 +136,15 @@ __device__ int g_device_error;
 }  // namespace
 
 namespace fdwt {
+// The address is looked up once per device (with that device current) under a lock and kept:
+// like every per-device cache of this library it assumes the device's primary context lives
+// as long as the process (no cudaDeviceReset between calls).
 int* device_error_flag() {
+  static std::mutex mu;
   static int* cache[64] = {nullptr};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
   if (cache[dev] == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
@@ -147,7 +152,27 @@ int* device_error_flag() {
   }
   return cache[dev];
 }
+
+static std::atomic<unsigned> g_wait_extra_tx{0};
+static std::atomic<long long> g_wait_tries{kCopyWaitTries};
+
+CopyWaitTest copy_wait_test() {
+  return {g_wait_extra_tx.load(std::memory_order_relaxed),
+          g_wait_tries.load(std::memory_order_relaxed)};
+}
 }  // namespace fdwt
+
+static std::atomic<int> g_cwt_tile_test{0};
+int fdwt::cwt_tile_test() { return g_cwt_tile_test.load(std::memory_order_relaxed); }
+
+extern "C" void fdwt_set_cwt_tile_test(int t_len) {
+  g_cwt_tile_test.store(t_len > 0 ? t_len : 0, std::memory_order_relaxed);
+}
+
+extern "C" void fdwt_set_copy_wait_test(unsigned extra_tx_bytes, long long tries) {
+  fdwt::g_wait_extra_tx.store(extra_tx_bytes, std::memory_order_relaxed);
+  fdwt::g_wait_tries.store(tries > 0 ? tries : fdwt::kCopyWaitTries, std::memory_order_relaxed);
+}
 
 extern "C" int fdwt_device_error(int* code) {
   if (code == nullptr) return FDWT_ERR_INVALID;

@@ -57,6 +57,21 @@ int pre_launch(cudaStream_t stream);
 // fdwt_device_error() reads and clears it.
 int* device_error_flag();
 constexpr int kErrCopyTimeout = 1;
+// Poll limit of every bounded mbarrier wait of the streaming kernels.
+constexpr long long kCopyWaitTries = 1LL << 22;
+// Test hook of those waits (fdwt_set_copy_wait_test): `extra_tx` bytes the kernels add to the
+// expected transaction count of the copy of global tile 0 (its wait then runs out while every
+// issued copy still completes), and the poll limit of the main waits (`tries`).  The wait for
+// copies still in flight after a timeout polls max(tries, 2^20) times.  {0, kCopyWaitTries}
+// unless a test set them.
+struct CopyWaitTest {
+  unsigned extra_tx;
+  long long tries;
+};
+CopyWaitTest copy_wait_test();
+// Test hook of the Morlet kernels (fdwt_set_cwt_tile_test): when > 0, the forward and backward
+// passes run on time tiles of that many positions even where whole rows would fit.
+int cwt_tile_test();
 
 // ------------------------------------------------------------------------------ types
 template <typename T> struct AccOf { using type = float; };

@@ -70,6 +70,25 @@ int synthesis_levels(int levels, int64_t approx_len, const int64_t* coef_len,
   return FDWT_OK;
 }
 
+// Checks the arguments of an analysis call that do not point at device data, as
+// fdwt_dwt_analysis does, and stores the workspace its plan needs in *need.
+int analysis_need(int dtype, int64_t rows, int64_t n, int levels, const int64_t* coef_len,
+                  const int64_t* pad_last, int filter_len, int mode, int off, size_t* need) {
+  *need = 0;
+  if (rows < 0 || dtype < FDWT_F32 || dtype > FDWT_BF16) return FDWT_ERR_INVALID;
+  if (filter_len < 2 || (filter_len & 1)) return FDWT_ERR_INVALID;
+  const int LM = pick_lm(filter_len);
+  if (LM < 0) return FDWT_ERR_UNSUPPORTED;
+  std::vector<Level> lv;
+  const int st = analysis_levels(n, levels, coef_len, pad_last, mode, lv, nullptr);
+  if (st != FDWT_OK) return st;
+  return dispatch<true>(dtype, LM, rows, static_cast<const void*>(nullptr), lv,
+                        static_cast<void*>(nullptr), static_cast<const double*>(nullptr),
+                        static_cast<const double*>(nullptr), filter_len, off,
+                        static_cast<void*>(nullptr), size_t(0),
+                        static_cast<cudaStream_t>(nullptr), need);
+}
+
 }  // namespace
 }  // namespace dwtk
 }  // namespace fdwt
@@ -101,16 +120,10 @@ extern "C" int fdwt_dwt_analysis(int dtype, int64_t rows, const void* x, int64_t
 extern "C" size_t fdwt_dwt_analysis_workspace(int dtype, int64_t rows, int64_t n, int levels,
                                               const int64_t* coef_len, const int64_t* pad_last,
                                               int filter_len, int mode, int off) {
-  const int LM = pick_lm(filter_len);
-  if (LM < 0 || rows < 0) return 0;
-  std::vector<Level> lv;
-  if (analysis_levels(n, levels, coef_len, pad_last, mode, lv, nullptr) != FDWT_OK) return 0;
   size_t need = 0;
-  dispatch<true>(dtype, LM, rows, static_cast<const void*>(nullptr), lv,
-                   static_cast<void*>(nullptr), static_cast<const double*>(nullptr),
-                   static_cast<const double*>(nullptr), filter_len, off,
-                   static_cast<void*>(nullptr), size_t(0), static_cast<cudaStream_t>(nullptr),
-                   &need);
+  if (analysis_need(dtype, rows, n, levels, coef_len, pad_last, filter_len, mode, off, &need) !=
+      FDWT_OK)
+    return 0;
   return need;
 }
 
@@ -201,16 +214,22 @@ extern "C" int fdwt_dwt_analysis_noalloc(int dtype, int64_t rows, const void* x,
                                          const int64_t* pad_last, void* const* out,
                                          const double* h0, const double* h1, int filter_len,
                                          int mode, int off, void* stream) {
-  const size_t need = fdwt_dwt_analysis_workspace(dtype, rows, n, levels, coef_len, pad_last,
-                                                  filter_len, mode, off);
+  if (out == nullptr || h0 == nullptr || h1 == nullptr) return FDWT_ERR_INVALID;
+  // one validation of the arguments, which also sizes the plan's workspace (it covers every
+  // plan the call may take at run time, e.g. the one for an x that is not 16-byte aligned)
+  size_t need = 0;
+  const int st = analysis_need(dtype, rows, n, levels, coef_len, pad_last, filter_len, mode, off,
+                               &need);
+  if (st != FDWT_OK) return st;
   if (need > kNoAllocScratchBytes) return FDWT_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   if (need > 0) {
-    const int st = noalloc_scratch(&scratch);
-    if (st != FDWT_OK) return st;
+    const int sc = noalloc_scratch(&scratch);
+    if (sc != FDWT_OK) return sc;
   }
   // Every element of a handover region is written by one launch before the next launch reads
   // it, so nothing left in the array by an earlier call needs clearing.
   return fdwt_dwt_analysis(dtype, rows, x, n, levels, coef_len, pad_last, out, h0, h1,
-                           filter_len, mode, off, scratch, need, stream);
+                           filter_len, mode, off, scratch, scratch ? kNoAllocScratchBytes : 0,
+                           stream);
 }

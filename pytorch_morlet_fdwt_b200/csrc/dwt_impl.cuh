@@ -1054,8 +1054,19 @@ int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
   using C = Cfg<T, LM>;
   const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
   if (ANALYSIS && allow_stream) {
+    size_t stream_need = 0;
     const int sa = run_ana_stages<T, LM>(rows, src0, lv, dst_final, h0, h1, L, off, ws, ws_bytes,
-                                         stream, ws_needed);
+                                         stream, ws_needed ? &stream_need : nullptr);
+    if (ws_needed != nullptr && sa == FDWT_OK) {
+      // At run time an x that is not 16-byte aligned does not stream: the call then takes the
+      // cluster plan below, so the query covers both plans.
+      size_t cluster_need = 0;
+      if (run<T, LM, true>(rows, src0, lv, dst_final, h0, h1, L, off, nullptr, 0, stream,
+                           &cluster_need, false) != FDWT_OK)
+        cluster_need = 0;
+      *ws_needed = std::max(stream_need, cluster_need);
+      return FDWT_OK;
+    }
     if (sa != FDWT_ERR_UNSUPPORTED) return sa;
   }
   if (!ANALYSIS) {

@@ -27,7 +27,7 @@ namespace dwtk {
 
 constexpr int SNT = 256;             // threads per streaming CTA
 constexpr int kStreamStages = 3;     // ring slots (tiles in flight per CTA)
-constexpr long long kStreamWaitTries = 1LL << 22;
+constexpr long long kStreamWaitTries = kCopyWaitTries;
 constexpr int kFillNone = 0, kFillZero = 1, kFillPeriodic = 2;
 
 template <typename A, int LM>
@@ -36,6 +36,8 @@ struct StreamParams {
   const A* d;        // (rows, nc) details
   A* y;              // (rows, n_out)
   int* err;          // device error word
+  uint32_t dbg_tx;   // test hook: extra expected bytes of global tile 0's copy
+  long long tries;   // poll limit of the main mbarrier waits
   int64_t a_stride;
   int64_t ntile;     // rows * ni interior tiles
   int32_t nc, n_out, off, ni, t_lo;
@@ -68,10 +70,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-  for (long long i = 0; i < kStreamWaitTries; ++i)
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity,
+                                                  long long tries) {
+  for (long long i = 0; i < tries; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
+}
+// Poll limit of the wait for a CTA's copies still in flight after a timeout: never shorter than
+// 2^20 polls, so that a shortened test limit cannot end a CTA while its copies still land.
+__device__ __forceinline__ long long cleanup_tries(long long tries) {
+  return tries > (1LL << 20) ? tries : (1LL << 20);
 }
 // global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes,
@@ -170,7 +178,7 @@ __device__ void stream_tiles(const StreamParams<A, LM>& p, A* ring, uint64_t* ba
     const int pre = p.fill == kFillPeriodic ? max(0, -glo) : 0;
     const int suf = p.fill == kFillPeriodic ? max(0, glo + span - nc) : 0;
     const unsigned tx = static_cast<unsigned>(max(hi - lo, 0) + pre + suf) * sizeof(A);
-    mbar_expect_tx(&bar[s], 2 * tx);
+    mbar_expect_tx(&bar[s], 2 * tx + (g == 0 ? p.dbg_tx : 0u));
     const A* src[2] = {p.a + row * p.a_stride, p.d + row * nc};
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -198,7 +206,7 @@ __device__ void stream_tiles(const StreamParams<A, LM>& p, A* ring, uint64_t* ba
   for (int64_t g = blockIdx.x; g < p.ntile; g += G, ++k) {
     const int s = k % kStreamStages;
     const unsigned par = static_cast<unsigned>(k / kStreamStages) & 1u;
-    const bool ok = mbar_wait_bounded(&bar[s], par);
+    const bool ok = mbar_wait_bounded(&bar[s], par, p.tries);
     if (ok) {
       const int64_t row = g / p.ni;
       const int t = p.t_lo + static_cast<int>(g % p.ni);
@@ -232,7 +240,8 @@ __device__ void stream_tiles(const StreamParams<A, LM>& p, A* ring, uint64_t* ba
           if (gj >= p.ntile) break;
           const int kj = k + j;
           mbar_wait_bounded(&bar[kj % kStreamStages],
-                            static_cast<unsigned>(kj / kStreamStages) & 1u);
+                            static_cast<unsigned>(kj / kStreamStages) & 1u,
+                            cleanup_tries(p.tries));
         }
       }
       return;
@@ -332,6 +341,11 @@ int run_syn_stream(int64_t rows, const void* a, const Level& L0, void* y, const 
     p.y = static_cast<A*>(y);
     p.err = device_error_flag();
     if (p.err == nullptr) return FDWT_ERR_CUDA;
+    {
+      const CopyWaitTest wt = copy_wait_test();
+      p.dbg_tx = wt.extra_tx;
+      p.tries = wt.tries;
+    }
     p.a_stride = a_stride;
     p.ntile = rows * ni;
     p.nc = static_cast<int>(nc);
@@ -396,6 +410,8 @@ struct AnaStreamParams {
   A* ap;             // (rows, a_len) approximation (a_len = nc or nc + 1: trailing zero)
   A* dp;             // (rows, nc) details
   int* err;          // device error word
+  uint32_t dbg_tx;   // test hook: extra expected bytes of global tile 0's copy
+  long long tries;   // poll limit of the main mbarrier waits
   int64_t ntile;     // rows * tiles
   int64_t P;         // period of the boundary mode
   int32_t n, nc, a_len, off, mode, tiles, span;
@@ -499,7 +515,7 @@ __device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint6
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
     const int lo = max(xlo, 0), hi = min(xlo + span, n);
     const unsigned bytes = static_cast<unsigned>(max(hi - lo, 0)) * sizeof(A);
-    mbar_expect_tx(&bar[s], bytes);
+    mbar_expect_tx(&bar[s], bytes + (g == 0 ? p.dbg_tx : 0u));
     if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * n + lo, bytes, &bar[s]);
   };
   // the gathers of tile k form the k-th commit group of every thread; the group of tile k + 1
@@ -524,7 +540,7 @@ __device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint6
   for (int64_t g = blockIdx.x; g < p.ntile; g += G, ++k) {
     const int s = k % kStreamStages;
     const unsigned par = static_cast<unsigned>(k / kStreamStages) & 1u;
-    const bool ok = mbar_wait_bounded(&bar[s], par);
+    const bool ok = mbar_wait_bounded(&bar[s], par, p.tries);
     if (ok) {
       const int64_t row = g / p.tiles;
       const int t = static_cast<int>(g % p.tiles);
@@ -555,7 +571,8 @@ __device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint6
           if (gj >= p.ntile) break;
           const int kj = k + j;
           mbar_wait_bounded(&bar[kj % kStreamStages],
-                            static_cast<unsigned>(kj / kStreamStages) & 1u);
+                            static_cast<unsigned>(kj / kStreamStages) & 1u,
+                            cleanup_tries(p.tries));
         }
       }
       return;
@@ -637,6 +654,11 @@ int run_ana_stream(int64_t rows, const void* x, const Level& L0, void* a_out, co
     p.dp = static_cast<A*>(L0.detail);
     p.err = device_error_flag();
     if (p.err == nullptr) return FDWT_ERR_CUDA;
+    {
+      const CopyWaitTest wt = copy_wait_test();
+      p.dbg_tx = wt.extra_tx;
+      p.tries = wt.tries;
+    }
     p.ntile = rows * tiles;
     p.P = L0.P;
     p.n = static_cast<int>(L0.n_in);

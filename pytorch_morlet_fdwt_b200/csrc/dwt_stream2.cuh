@@ -39,6 +39,8 @@ struct Ana2Params {
   A* a2;             // (rows, a_len2) level-(k+1) approximation
   A* d2;             // (rows, nc2) level-(k+1) details
   int* err;          // device error word
+  uint32_t dbg_tx;   // test hook: extra expected bytes of global tile 0's copy
+  long long tries;   // poll limit of the main mbarrier waits
   int64_t ntile;     // rows * tiles
   int64_t P;         // period of level k's boundary mode on n
   int64_t P2;        // period of level k+1's boundary mode on n1
@@ -85,7 +87,7 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
     const int lo = max(xlo, 0), hi = min(xlo + span, n);
     const unsigned bytes = static_cast<unsigned>(max(hi - lo, 0)) * sizeof(A);
-    mbar_expect_tx(&bar[s], bytes);
+    mbar_expect_tx(&bar[s], bytes + (g == 0 ? p.dbg_tx : 0u));
     if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * n + lo, bytes, &bar[s]);
   };
 #pragma unroll 1
@@ -108,7 +110,7 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
   for (int64_t g = blockIdx.x; g < p.ntile; g += G, ++k) {
     const int s = k % ana2_stages<A>();
     const unsigned par = static_cast<unsigned>(k / ana2_stages<A>()) & 1u;
-    const bool ok = mbar_wait_bounded(&bar[s], par);
+    const bool ok = mbar_wait_bounded(&bar[s], par, p.tries);
     const int64_t row = g / p.tiles;
     const int t = static_cast<int>(g % p.tiles);
     const int o1_0 = first_o1(t);
@@ -171,7 +173,8 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
           if (gj >= p.ntile) break;
           const int kj = k + j;
           mbar_wait_bounded(&bar[kj % ana2_stages<A>()],
-                            static_cast<unsigned>(kj / ana2_stages<A>()) & 1u);
+                            static_cast<unsigned>(kj / ana2_stages<A>()) & 1u,
+                            cleanup_tries(p.tries));
         }
       }
       return;
@@ -325,6 +328,11 @@ int run_ana2_stream(int64_t rows, const void* x, const Level& L1, const Level& L
     p.d2 = static_cast<A*>(L2.detail);
     p.err = device_error_flag();
     if (p.err == nullptr) return FDWT_ERR_CUDA;
+    {
+      const CopyWaitTest wt = copy_wait_test();
+      p.dbg_tx = wt.extra_tx;
+      p.tries = wt.tries;
+    }
     for (int j = 0; j < LM; ++j) {
       p.taps[2 * j] = j < L ? static_cast<A>(h0[j]) : A(0);
       p.taps[2 * j + 1] = j < L ? static_cast<A>(h1[j]) : A(0);
@@ -363,6 +371,8 @@ struct Syn2Params {
   const A* d1;       // (rows, nc1)
   A* y;              // (rows, n_out)
   int* err;          // device error word
+  uint32_t dbg_tx;   // test hook: extra expected bytes of global tile 0's copy
+  long long tries;   // poll limit of the main mbarrier waits
   int64_t a2_stride;
   int64_t ntile;     // rows * tiles
   int32_t nc2, nc1, n_out, off, fill, tiles, T;
@@ -429,7 +439,8 @@ __device__ void syn2_tiles(const Syn2Params<A, LM>& p, A* ring, A* abuf, uint64_
     const int64_t row = g / p.tiles;
     const int t = static_cast<int>(g % p.tiles);
     const int gl = glo_of(t), g2 = g2lo_of(t);
-    mbar_expect_tx(&bar[s], tx_range(gl, span, p.nc1) + 2 * tx_range(g2, span2, p.nc2));
+    mbar_expect_tx(&bar[s], tx_range(gl, span, p.nc1) + 2 * tx_range(g2, span2, p.nc2) +
+                                (g == 0 ? p.dbg_tx : 0u));
     A* d1s = slot(s);
     copy_range(d1s, p.d1 + row * p.nc1, gl, span, p.nc1, s);
     copy_range(d1s + span, p.a2 + row * p.a2_stride, g2, span2, p.nc2, s);
@@ -453,7 +464,7 @@ __device__ void syn2_tiles(const Syn2Params<A, LM>& p, A* ring, A* abuf, uint64_
   for (int64_t g = blockIdx.x; g < p.ntile; g += G, ++k) {
     const int s = k % kStreamStages;
     const unsigned par = static_cast<unsigned>(k / kStreamStages) & 1u;
-    const bool ok = mbar_wait_bounded(&bar[s], par);
+    const bool ok = mbar_wait_bounded(&bar[s], par, p.tries);
     const int64_t row = g / p.tiles;
     const int t = static_cast<int>(g % p.tiles);
     const int gl = glo_of(t);
@@ -518,7 +529,8 @@ __device__ void syn2_tiles(const Syn2Params<A, LM>& p, A* ring, A* abuf, uint64_
           if (gj >= p.ntile) break;
           const int kj = k + j;
           mbar_wait_bounded(&bar[kj % kStreamStages],
-                            static_cast<unsigned>(kj / kStreamStages) & 1u);
+                            static_cast<unsigned>(kj / kStreamStages) & 1u,
+                            cleanup_tries(p.tries));
         }
       }
       return;
@@ -655,6 +667,11 @@ int run_syn2_stream(int64_t rows, const void* a2, const Level& Lc, const Level& 
     p.y = static_cast<A*>(y);
     p.err = device_error_flag();
     if (p.err == nullptr) return FDWT_ERR_CUDA;
+    {
+      const CopyWaitTest wt = copy_wait_test();
+      p.dbg_tx = wt.extra_tx;
+      p.tries = wt.tries;
+    }
     A hh0[LM], hh1[LM];
     for (int j = 0; j < LM; ++j) {
       hh0[j] = j < L ? static_cast<A>(h0[j]) : A(0);

@@ -26,7 +26,6 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 from torch import nn
-from torch.autograd.function import once_differentiable
 
 from . import _lib
 
@@ -444,6 +443,62 @@ class CWT1D(nn.Module):
 
 
 # --------------------------------------------------------------------------- fused consumers
+#
+# Higher-order derivatives.  The fused kernels' backward passes return first derivatives only.
+# When a backward runs with create_graph=True, the two consumers below instead recompute their
+# output through the transform node (whose derivatives of every order come from the forward,
+# adjoint and filter-gradient kernels) followed by the consumer written with torch ops, and take
+# the gradient of that graph with create_graph=True: the scalogram is materialised for that
+# call only.  The reference's CPU path gets the same derivatives from autograd
+# (fdwt/cwt.py:391-394, 545-549).
+
+
+def _scalogram_magnitude(W: torch.Tensor, plan: "MorletPlan") -> torch.Tensor:
+    """``|W|`` of a ``(R, S, N, C)`` transform output, as torch's complex ``abs``."""
+    if plan.channels == 2:
+        return torch.view_as_complex(W).abs()
+    return W[..., 0].abs()
+
+
+def _mix_composed(x, plan, H, a, b):
+    """``sum_s a[d, s] |W_s| + b[d, s] Re W_s`` on rows ``x (R, N)`` through the transform node."""
+    W = _MorletCWTFunction.apply(x, plan, H)
+    R, S, N, _ = W.shape
+    D = a.shape[0]
+    mag = _scalogram_magnitude(W, plan).view(R // D, D, S, N)
+    re = W[..., 0].view(R // D, D, S, N)
+    y = torch.einsum("bdsn,ds->bdn", mag, a.to(W.dtype)) + \
+        torch.einsum("bdsn,ds->bdn", re, b.to(W.dtype))
+    return y.reshape(R, N)
+
+
+def _softmax_composed(x, plan, H, V, nch, tau):
+    """``sum_f softmax_f(|W_f| / tau) V_f`` on rows ``x (R, N)`` through the transform node."""
+    W = _MorletCWTFunction.apply(x, plan, H)
+    R = W.shape[0]
+    p = torch.softmax(_scalogram_magnitude(W, plan) / tau, dim=1)  # (R, S, N)
+    Vd = V.to(W.dtype)
+    Vr = Vd.repeat(R // nch, 1)[:, :, None] if Vd.dim() == 2 else \
+        Vd.repeat_interleave(nch, dim=0)
+    return (p * Vr).sum(1)
+
+
+def _recomputed_grads(ctx, gy, inputs, fn, slots):
+    """Gradients of ``fn(*inputs)`` against ``gy`` with create_graph=True, placed in the
+    Function's argument slots ``slots`` (the other slots get None)."""
+    needs = [ctx.needs_input_grad[k] for k in slots]
+    with torch.enable_grad():
+        y = fn(*inputs)
+        wrt = [t for t, n in zip(inputs, needs) if n]
+        grads = iter(torch.autograd.grad(y, wrt, gy, create_graph=True, allow_unused=True)
+                     if wrt else [])
+    out = [None] * (max(slots) + 1)
+    for k, t, n in zip(slots, inputs, needs):
+        if n:
+            g = next(grads)
+            out[k] = torch.zeros_like(t) if g is None else g.to(t.dtype)
+    return tuple(out)
+
 
 
 def _mix_forward(x2, plan, H, a, b):
@@ -504,9 +559,11 @@ class _MorletMixFunction(torch.autograd.Function):
         return _mix_forward(x, plan, H, a, b)
 
     @staticmethod
-    @once_differentiable
     def backward(ctx, gy):
         x, H, a, b = ctx.saved_tensors
+        if torch.is_grad_enabled():  # create_graph: gradients that are differentiable again
+            return _recomputed_grads(ctx, gy, (x, H, a, b), lambda x_, H_, a_, b_: _mix_composed(
+                x_, ctx.plan, H_, a_, b_), (0, 2, 3, 4))
         need_h = ctx.needs_input_grad[2]
         gx, gH, ga, gb = _mix_backward(gy, x, ctx.plan, H, a, b, ctx.needs_input_grad[0],
                                        need_h)
@@ -585,9 +642,12 @@ class _SpectralSoftmaxFunction(torch.autograd.Function):
         return out
 
     @staticmethod
-    @once_differentiable
     def backward(ctx, gy):
         x, H, V, m, l, out = ctx.saved_tensors
+        if torch.is_grad_enabled():  # create_graph: gradients that are differentiable again
+            return _recomputed_grads(
+                ctx, gy, (x, H, V), lambda x_, H_, V_: _softmax_composed(
+                    x_, ctx.plan, H_, V_, ctx.nch, ctx.tau), (0, 2, 3)) + (None, None, None)
         need_h = ctx.needs_input_grad[2]
         gx, gH, gV = _softmax_backward(gy, x, ctx.plan, H, V, ctx.nch, ctx.tau, m, l, out,
                                        ctx.needs_input_grad[0], need_h)

@@ -10,7 +10,9 @@ whole multilevel transform is ONE autograd node and one C-ABI call
 levels as a short chain of streaming launches:
 
 * :class:`_AnalysisFn` -- multilevel analysis ``A``; its backward is :class:`_SynthesisFn`;
-* :class:`_SynthesisFn` -- the exact transpose ``A^T``; its backward is :class:`_AnalysisFn`.
+* :class:`_SynthesisFn` -- the exact transpose ``A^T``; its backward is :class:`_AnalysisFn`;
+* :class:`_Analysis` / :class:`_Synthesis` -- the reference's per-level nodes with their
+  ``apply`` signatures (``dwt.py:36-82``), each one single-level C-ABI call.
 
 ``wavedec`` is ``A`` with the ``dec_*`` filters; its gradient is ``A^T``.  ``idwt`` /
 ``waverec`` are ``A^T`` of a zero-mode (or periodization) analysis on the time-reversed
@@ -28,7 +30,7 @@ from typing import List, Optional, Sequence, Tuple
 import torch
 from torch import nn
 
-from . import _lib
+from . import _lib, config
 from .wavelets import WaveletLike, get_filter_bank
 
 __all__ = ["dwt", "idwt", "wavedec", "waverec", "dwt_max_level", "dwt_coeff_len", "DWT1D",
@@ -129,6 +131,8 @@ def _analysis(x: torch.Tensor, spec: _Spec) -> List[torch.Tensor]:
             h0, h1, L, spec.mode, spec.off,
             None if ws is None else ws.data_ptr(), nws, _lib.stream_of(dev))
     _lib.check(st, "fdwt_dwt_analysis")
+    if config.check_device_errors:
+        _lib.check_device_error("fdwt_dwt_analysis")
     return [o.reshape(*lead, o.shape[-1]) for o in outs]
 
 
@@ -159,13 +163,16 @@ def _synthesis(inputs: Sequence[Optional[torch.Tensor]], spec: _Spec) -> torch.T
             h0, h1, L, spec.mode, spec.off,
             None if ws is None else ws.data_ptr(), nws, _lib.stream_of(dev))
     _lib.check(st, "fdwt_dwt_synthesis")
+    if config.check_device_errors:
+        _lib.check_device_error("fdwt_dwt_synthesis")
     return y.reshape(*lead, spec.n)
 
 
 class _AnalysisFn(torch.autograd.Function):
     """``(approx, d_J..d_1) = A x`` for a whole multilevel transform; backward = ``A^T``.
 
-    Replaces the per-level ``_Analysis`` node of the reference (``dwt.py:36-56``)."""
+    The multilevel counterpart of :class:`_Analysis`: ``wavedec`` runs every level in one
+    node (the reference chains one ``_Analysis`` per level, ``fdwt/dwt.py:146-158``)."""
 
     @staticmethod
     def forward(ctx, x, spec: _Spec):
@@ -183,7 +190,8 @@ class _AnalysisFn(torch.autograd.Function):
 class _SynthesisFn(torch.autograd.Function):
     """``y = A^T (approx, d_J..d_1)``; backward = ``A``.
 
-    Replaces the per-level ``_Synthesis`` node of the reference (``dwt.py:59-82``)."""
+    The multilevel counterpart of :class:`_Synthesis`: ``waverec`` runs every level in one
+    node (the reference chains one ``_Synthesis`` per level, ``fdwt/dwt.py:161-171``)."""
 
     @staticmethod
     def forward(ctx, spec: _Spec, *inputs):
@@ -198,6 +206,71 @@ class _SynthesisFn(torch.autograd.Function):
             return (None,) * (1 + len(ctx.present))
         grads = _AnalysisFn.apply(gy.contiguous(), ctx.spec)
         return (None,) + tuple(g if p else None for g, p in zip(grads, ctx.present))
+
+
+def _taps(h: torch.Tensor) -> Tuple[float, ...]:
+    """Filter taps of a 1-D tensor as the host doubles the C ABI takes."""
+    return tuple(float(v) for v in h.detach().reshape(-1).double().cpu().tolist())
+
+
+def _one_level_spec(h0, h1, mode: int, off: int, n: int, n_out: int) -> _Spec:
+    if len(h0) != len(h1) or len(h0) % 2:
+        raise ValueError("h0 and h1 must have the same even length")
+    return _Spec(_taps(h0), _taps(h1), int(mode), int(off), int(n), (int(n_out),), (0,))
+
+
+class _Analysis(torch.autograd.Function):
+    """One level ``(y0, y1) = A x``; backward ``A^T`` through :class:`_Synthesis`.
+
+    Same ``apply(x, h0, h1, mode, off, n_out)`` as the reference's per-level node
+    (``fdwt/dwt.py:36-56``): ``h0``/``h1`` are the (even-length) filter tensors, ``mode`` the
+    integer of ``MODES``, ``off`` the phase offset (1, or ``L // 2`` for periodization) and
+    ``n_out`` the coefficient length.  One ``fdwt_dwt_analysis`` call with one level."""
+
+    @staticmethod
+    def forward(ctx, x, h0, h1, mode: int, off: int, n_out: int):
+        spec = _one_level_spec(h0, h1, mode, off, x.shape[-1], n_out)
+        ctx.save_for_backward(h0, h1)
+        ctx.cfg = (mode, off, x.shape[-1])
+        a, d = _analysis(x, spec)
+        return a, d
+
+    @staticmethod
+    def backward(ctx, g0, g1):
+        h0, h1 = ctx.saved_tensors
+        mode, off, n = ctx.cfg
+        gx = None
+        if ctx.needs_input_grad[0] and (g0 is not None or g1 is not None):
+            g0 = torch.zeros_like(g1) if g0 is None else g0
+            g1 = torch.zeros_like(g0) if g1 is None else g1
+            gx = _Synthesis.apply(g0, g1, h0, h1, mode, off, n)
+        return gx, None, None, None, None, None
+
+
+class _Synthesis(torch.autograd.Function):
+    """One level ``y = A^T (a, d)``; backward ``A`` through :class:`_Analysis`.
+
+    Same ``apply(a, d, h0, h1, mode, off, n)`` as the reference's per-level node
+    (``fdwt/dwt.py:59-82``); ``n`` is the output length.  One ``fdwt_dwt_synthesis`` call with
+    one level."""
+
+    @staticmethod
+    def forward(ctx, a, d, h0, h1, mode: int, off: int, n: int):
+        if a.shape != d.shape:
+            raise ValueError(f"cA and cD shapes differ: {tuple(a.shape)} vs {tuple(d.shape)}")
+        spec = _one_level_spec(h0, h1, mode, off, n, a.shape[-1])
+        ctx.save_for_backward(h0, h1)
+        ctx.cfg = (mode, off, a.shape[-1])
+        return _synthesis([a, d], spec)
+
+    @staticmethod
+    def backward(ctx, gy):
+        h0, h1 = ctx.saved_tensors
+        mode, off, nc = ctx.cfg
+        ga = gd = None
+        if gy is not None and (ctx.needs_input_grad[0] or ctx.needs_input_grad[1]):
+            ga, gd = _Analysis.apply(gy, h0, h1, mode, off, nc)
+        return ga, gd, None, None, None, None, None
 
 
 def _bank(wavelet):

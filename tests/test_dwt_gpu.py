@@ -298,3 +298,59 @@ def test_one_level_analysis_long_rows(wname, mode, n, dtype, tol):
         close(c.grad, r, tol)
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_per_level_nodes_apply_vs_golden(mode):
+    """The reference's per-level autograd nodes, called through ``apply`` with the reference's
+    signatures (``fdwt/dwt.py:36-82``): ``_Analysis.apply(x, h0, h1, mode, off, n_out)`` gives
+    pywt's dwt, ``_Synthesis.apply(a, d, rec_lo[::-1], rec_hi[::-1], mode, off, n)`` pywt's idwt
+    (zero mode, or periodization), and their gradients match the fixtures."""
+    from pytorch_morlet_fdwt_b200.dwt import MODES as IDS, _Analysis, _Synthesis, dwt_coeff_len
+    g = golden("dwt_single")
+    for bname in ["haar", "db4", "rand5"]:
+        bank = F.get_filter_bank(bank_from_golden(bname))
+        L = bank.length
+        h0, h1 = gpu(bank.dec_lo), gpu(bank.dec_hi)
+        r0, r1 = gpu(bank.rec_lo[::-1]), gpu(bank.rec_hi[::-1])
+        off = L // 2 if mode == "periodization" else 1
+        for n in [7, 16, 33, 100]:
+            key = f"{bname}|{mode}|{n}"
+            x = gpu(g[key + "|x"]).requires_grad_()
+            n_out = dwt_coeff_len(n, L, mode)
+            a, d = _Analysis.apply(x, h0, h1, IDS[mode], off, n_out)
+            close(a, g[key + "|a"], 1e-12, 1.0)
+            close(d, g[key + "|d"], 1e-12, 1.0)
+            (a.square().sum() + 3.0 * d.square().sum()).backward()
+            close(x.grad, g[key + "|gx"], 1e-12, 1.0)
+            if key + "|y" not in g:
+                continue
+            if mode == "periodization":
+                sm, soff, ny = IDS["periodization"], L // 2, 2 * n_out
+            else:
+                sm, soff, ny = IDS["zero"], 1, 2 * n_out - L + 2
+            ag = a.detach().clone().requires_grad_()
+            dg = d.detach().clone().requires_grad_()
+            y = _Synthesis.apply(ag, dg, r0, r1, sm, soff, ny)
+            close(y, g[key + "|y"], 1e-12, 1.0)
+            y.square().sum().backward()
+            close(ag.grad, g[key + "|ga"], 1e-12, 1.0)
+            close(dg.grad, g[key + "|gd"], 1e-12, 1.0)
+
+
+@pytest.mark.parametrize("mode", ["symmetric", "periodization"])
+def test_misaligned_rows_on_a_multi_launch_length(mode):
+    """A contiguous view at an odd storage offset (rows not 16-byte aligned) does not stream and
+    falls back to the cluster plan at run time; the workspace the query returned covers it."""
+    torch.manual_seed(21)
+    bank = F.get_filter_bank("db8")
+    rows, n = 16, 1 << 18
+    flat = torch.randn(1 + rows * n, device=DEV)
+    x = flat[1:].view(rows, n)
+    assert x.data_ptr() % 16 != 0
+    got = F.wavedec(x, bank, mode, 8)
+    ref = F.wavedec(x.clone(), bank, mode, 8)
+    for g, r in zip(got, ref):
+        close(g, r, 1e-5)
+    y = F.waverec(got, bank, mode)
+    close(y[..., :n], x, 1e-5)

@@ -107,3 +107,24 @@ def test_noalloc_rejects_sizes_beyond_the_scratch():
     assert st == FDWT_ERR_SCRATCH_LIMIT
     assert b"no-allocation" in _lib.load().fdwt_status_string(st)
     assert _lib.launch_count() == before
+
+
+@pytest.mark.parametrize("mode", ["symmetric", "periodization"])
+def test_noalloc_misaligned_rows_match(mode):
+    """Rows that start 4 bytes past a 16-byte boundary (a contiguous view at an odd storage
+    offset) cannot stream; the call takes the cluster plan, whose workspace the query and the
+    static array must cover as well."""
+    torch.manual_seed(12)
+    bank = F.get_filter_bank("db4")
+    rows, level = 2, 10
+    n = _multi_launch_length(torch.float32, rows, bank, mode, level)
+    for call in range(2):
+        flat = torch.randn(1 + rows * n, dtype=torch.float32, device=DEV) * (call + 1)
+        x = flat[1:].view(rows, n)
+        assert x.data_ptr() % 16 != 0
+        st, need, outs = _call(x, bank, mode, level)
+        _lib.check(st, "fdwt_dwt_analysis_noalloc")
+        assert 0 < need <= SCRATCH_LIMIT
+        ref = F.wavedec(x.clone(), bank, mode, level)  # aligned copy
+        for o, r in zip(outs, ref):
+            _close(o, r, 1e-5)
