@@ -74,6 +74,11 @@ int fdwt_device_error(int* code);
  * allocation-free scratch) assume each device's primary context lives as long as the process
  * (no cudaDeviceReset between calls). */
 void fdwt_set_copy_wait_test(unsigned int extra_tx_bytes, long long tries);
+/* Test hook of the Morlet kernels (no counterpart in the reference).  While t_len > 0 every
+ * Morlet forward and backward call runs on time tiles of t_len positions, the path rows too
+ * long for one CTA's shared memory take, even where whole rows would fit (tests compare the
+ * two paths).  Process-wide; 0 restores the automatic choice. */
+void fdwt_set_cwt_tile_test(int t_len);
 
 /* ------------------------------------------------------------------------------------------
  * Discrete wavelet transform.  One call runs every level of a multilevel transform (the
@@ -182,6 +187,12 @@ typedef struct {
   int32_t support[FDWT_MAX_SCALES];     /* half-support (taps) of order[k] */
   double lowpass[FDWT_MAX_LOWPASS];     /* the full half-band filter, 2*c_lp+1 taps */
 } fdwt_morlet_plan;
+
+/* Row length.  A row whose pyramid buffers fit one CTA's shared memory is computed by one CTA;
+ * longer rows run on time tiles whose buffers reach the pyramid's dependency cone past both ends
+ * of the tile (forward), or as one launch per octave over tiles with the half-band chain's
+ * gradient handed between octaves through the workspace (backward).  Any n up to 2^30 - 1 is
+ * accepted; the workspace queries size both cases. */
 
 /* Forward transform: y (rows, n_scales, n, channels) from x (rows, n).  Replaces the
  * per-octave launches of the forward and half-band launchers (fdwt/kernels/conv.py:306-329,

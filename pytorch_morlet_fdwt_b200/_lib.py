@@ -31,6 +31,7 @@ SIGNATURES = {
     "fdwt_set_shared_memory_fill": (None, [ctypes.c_int, ctypes.c_uint]),
     "fdwt_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "fdwt_set_copy_wait_test": (None, [ctypes.c_uint, ctypes.c_longlong]),
+    "fdwt_set_cwt_tile_test": (None, [ctypes.c_int]),
     "fdwt_dwt_analysis_noalloc": (ctypes.c_int, [
         ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, c_i64p, c_i64p,
         c_voidpp, c_dblp, c_dblp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
@@ -188,6 +189,11 @@ def set_copy_wait_test(extra_tx_bytes: int, tries: int = 0) -> None:
     """Test hook: make the bounded copy wait of global tile 0 run out (see
     fdwt_set_copy_wait_test); ``(0, 0)`` restores the defaults."""
     load().fdwt_set_copy_wait_test(int(extra_tx_bytes), int(tries))
+
+
+def set_cwt_tile_test(t_len: int) -> None:
+    """Test hook: run every Morlet call on time tiles of ``t_len`` positions (0: automatic)."""
+    load().fdwt_set_cwt_tile_test(int(t_len))
 
 
 def set_shared_memory_fill(enable: bool, word: int = 0) -> None:

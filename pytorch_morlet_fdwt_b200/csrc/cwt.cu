@@ -1,7 +1,7 @@
 // C ABI of the Morlet CWT pyramid kernels (cwt_impl.cuh).  The computation type follows the
 // row type: fp32 rows compute in fp32, fp64 rows in fp64 (fp16/bf16 inputs are upcast to fp32
 // by the caller, as the reference does at fdwt/cwt.py:606-607).
-#include "cwt_bwd.cuh"
+#include "cwt_bwd_tiled.cuh"
 
 using namespace fdwt;
 using namespace fdwt::cwtk;

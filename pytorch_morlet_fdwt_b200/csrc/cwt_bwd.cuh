@@ -68,17 +68,33 @@ struct Cplx<double> {
 
 // ------------------------------------------------------------------------------ buffers
 
+// A shared buffer holding positions [-ext, n + ext) of a row (or of a tile's window): position
+// q at padded index sidx(q + ext).  Reads through ldE are clamped into that range.
+struct Win {
+  int n, ext;
+};
 template <typename A>
-__device__ __forceinline__ int clampE(const FwdParams<A>& f, int pos) {
-  return min(max(pos, -f.ext), static_cast<int>(f.n) + f.ext - 1);
+__device__ __forceinline__ Win win(const FwdParams<A>& f) {
+  return Win{static_cast<int>(f.n), f.ext};
+}
+__device__ __forceinline__ int clampE(const Win& w, int pos) {
+  return min(max(pos, -w.ext), w.n + w.ext - 1);
+}
+template <typename A>
+__device__ __forceinline__ A ldE(const Win& w, const A* buf, int pos) {
+  return buf[sidx<PS>(clampE(w, pos) + w.ext)];
+}
+template <typename A>
+__device__ __forceinline__ A& atE(const Win& w, A* buf, int pos) {
+  return buf[sidx<PS>(pos + w.ext)];
 }
 template <typename A>
 __device__ __forceinline__ A ldE(const FwdParams<A>& f, const A* buf, int pos) {
-  return buf[sidx<PS>(clampE(f, pos) + f.ext)];
+  return ldE(win(f), buf, pos);
 }
 template <typename A>
 __device__ __forceinline__ A& atE(const FwdParams<A>& f, A* buf, int pos) {
-  return buf[sidx<PS>(pos + f.ext)];
+  return atE(win(f), buf, pos);
 }
 
 // dL/dW buffer: positions [-1, n] (the two ends stay zero), complex values interleaved.
@@ -239,7 +255,7 @@ __device__ void bwd_lowpass_adjoint(const FwdParams<A>& f, const A* src, A* dst,
 
 // (re, im) of one scale at the P outputs n_i = base + dil i, windows read from X (clamped).
 template <typename A, bool SYM>
-__device__ __forceinline__ void conv_one(const FwdParams<A>& f, const A* X, const A* tab, int K,
+__device__ __forceinline__ void conv_one(const Win& f, const A* X, const A* tab, int K,
                                          int dil, int base, Acc2<A> (&acc)[P]) {
   A L[P], R[P];
 #pragma unroll
@@ -316,9 +332,9 @@ __device__ __forceinline__ void adjoint_taps(const A* tab, const A* gw, int n, i
 // G(p) += sum_k h_re(k) gWre(p + dk) + h_im(k) gWim(p + dk) for p in [pa, pb).  Items whose
 // whole window lies in [-1, n] skip the per-load clamp.
 template <typename A, int C, bool SYM>
-__device__ void adjoint_scale(const FwdParams<A>& f, const Oct& O, const A* tab, const A* gw,
+__device__ void adjoint_scale(const Win& f, const Oct& O, const A* tab, const A* gw,
                               A* G, int pa, int pb, int K) {
-  const int n = static_cast<int>(f.n);
+  const int n = f.n;
   const int dil = O.dil;
   const int len = pb - pa;
   if (len <= 0) return;
@@ -467,7 +483,7 @@ __device__ void make_gw(const BwdParams<A>& p, const Oct& O, int s, int gs, cons
     if (phi >= n) continue;
     const int base = phi + dil * u0;
     Acc2<A> acc[P];
-    conv_one<A, SYM>(f, X, tab, O.half, dil, base, acc);
+    conv_one<A, SYM>(win(f), X, tab, O.half, dil, base, acc);
 #pragma unroll
     for (int i = 0; i < P; ++i) {
       const int q = base + dil * i;
@@ -515,7 +531,7 @@ __device__ __forceinline__ void scale_grads(const BwdParams<A>& p, const Oct& O,
   const FwdParams<A>& f = p.f;
   if (p.need_gx) {  // the adjoint over the scale's nonzero taps (ks <= O.half) and their reach
     const int reach = min(live, ks * O.dil);
-    adjoint_scale<A, C, SYM>(f, O, tab, gw, G, -reach, static_cast<int>(f.n) + reach, ks);
+    adjoint_scale<A, C, SYM>(win(f), O, tab, gw, G, -reach, static_cast<int>(f.n) + reach, ks);
   }
   if (p.gh_part) {
     const int hcols = 2 * f.center + 1;
@@ -762,8 +778,47 @@ BwdLayout bwd_layout(int EPI, int64_t rows, int64_t n, const fdwt_morlet_plan* p
   return L;
 }
 
+// Shared bytes of the row-resident backward kernel for rows of n samples (the buffer offsets go
+// into p when it is given).
+template <typename A, int EPI>
+size_t row_bwd_smem(int64_t n, const fdwt_morlet_plan* pl, int ext, BwdParams<A>* p) {
+  const int64_t buf_len = padded_len<PS>(n + 2 * static_cast<int64_t>(ext)) + 8;
+  const int64_t gw_len = 2 * padded_len<PS>(n + 2) + 8;
+  if (buf_len > 0x3fffffffLL) return ~size_t(0);
+  size_t off = 3 * static_cast<size_t>(buf_len) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  const size_t gw_off = off;
+  off += (EPI == EPI_STORE ? 2 : 1) * static_cast<size_t>(gw_len) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  const size_t tab_off = off;
+  size_t tab = 0;  // the largest octave's tap tables
+  for (int j = 0; j < pl->n_octaves; ++j)
+    tab = std::max(tab, 4 * static_cast<size_t>(pl->oct_count[j]) * (pl->oct_half[j] + 1));
+  off += tab * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  const size_t red_off = off;
+  off += NW * sizeof(A);
+  if (p) {
+    p->f.buf_len = static_cast<int>(buf_len);
+    p->gw_len = static_cast<int>(gw_len);
+    p->gw_off = static_cast<int>(gw_off);
+    p->tab_off = static_cast<int>(tab_off);
+    p->red_off = static_cast<int>(red_off);
+  }
+  return off + 16;
+}
+
+template <typename A, int EPI>
+int run_backward_tiled(int64_t rows, int64_t n, const void* x, const void* h,
+                       const fdwt_morlet_plan* pl, const Geometry& geo, const void* a,
+                       const void* b, int64_t dim, int v_pos, double inv_tau, const void* g,
+                       const void* sm_m, const void* sm_l, const void* sm_out, void* gx, void* gh,
+                       void* ga, void* gb, void* gv, bool need_h, void* ws, size_t ws_bytes,
+                       cudaStream_t stream, size_t* ws_needed);
+
 // Backward of the transform (EPI_STORE), of the mix (EPI_MIX) or of the spectral softmax
-// (EPI_SOFTMAX).  Outputs gx (rows, n), gh (S*C, 2*center+1), ga/gb (dim, S), gv (nch, S) or
+// (EPI_SOFTMAX).  Rows whose buffers do not fit one CTA's shared memory take the octave-tiled
+// launches of cwt_bwd_tiled.cuh.  Outputs gx (rows, n), gh (S*C, 2*center+1), ga/gb (dim, S), gv (nch, S) or
 // (G, S, n); null outputs are skipped.  ws_needed != null: only report the workspace size (for
 // a call with or without gh, as need_h says).
 template <typename A, int EPI>
@@ -779,8 +834,16 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   const Geometry geo = geometry(pl);
   if (ws_needed == nullptr) need_h = gh != nullptr;
   if (v_pos && (dim < 1 || rows % dim != 0)) return FDWT_ERR_INVALID;
+  int E = 0;
+  for (int j = 0; j < pl->n_octaves; ++j) E = std::max(E, geo.live[j]);
+  const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
+  const bool tiled = cwt_tile_test() > 0 || row_bwd_smem<A, EPI>(n, pl, E + 1, nullptr) > budget;
   const BwdLayout lay = bwd_layout<A>(EPI, rows, n, pl, geo, need_h, dim, v_pos != 0);
   if (ws_needed) {
+    if (tiled)
+      return run_backward_tiled<A, EPI>(rows, n, x, h, pl, geo, a, b, dim, v_pos, inv_tau, g,
+                                        sm_m, sm_l, sm_out, gx, gh, ga, gb, gv, need_h, ws,
+                                        ws_bytes, stream, ws_needed);
     *ws_needed = lay.total;
     return FDWT_OK;
   }
@@ -811,6 +874,10 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
     if (v_pos && (st = zero(gv, static_cast<size_t>(rows / dim) * S * n * sizeof(A))) != FDWT_OK)
       return st;
   }
+  if (tiled)
+    return run_backward_tiled<A, EPI>(rows, n, x, h, pl, geo, a, b, dim, v_pos, inv_tau, g, sm_m,
+                                      sm_l, sm_out, gx, gh, ga, gb, gv, need_h, ws, ws_bytes,
+                                      stream, nullptr);
   if (lay.total > 0 && (ws == nullptr || ws_bytes < lay.total)) return FDWT_ERR_WORKSPACE;
   unsigned char* w = static_cast<unsigned char*>(ws);
   A* pyr = reinterpret_cast<A*>(w);
@@ -822,8 +889,6 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
 
   BwdParams<A> p{};
   fill_common(p.f, pl, geo, n);
-  int E = 0;
-  for (int j = 0; j < pl->n_octaves; ++j) E = std::max(E, geo.live[j]);
   p.f.ext = E + 1;
   p.f.rows = rows;
   p.f.x = x;
@@ -833,7 +898,6 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   p.f.dim = dim;
   p.f.v_pos = v_pos;
   p.f.inv_tau = static_cast<A>(inv_tau);
-  p.f.buf_len = static_cast<int>(padded_len<PS>(n + 2 * static_cast<int64_t>(p.f.ext)) + 8);
   p.g = static_cast<const A*>(g);
   p.sm_m = static_cast<const A*>(sm_m);
   p.sm_l = static_cast<const A*>(sm_l);
@@ -848,22 +912,7 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   for (int j = 0; j < kMaxOct; ++j) p.pyr_off[j] = lay.pyr_off[j];
   p.need_gx = gx != nullptr;
   p.need_x = (gh != nullptr || EPI != EPI_STORE) ? 1 : 0;
-  p.gw_len = static_cast<int>(2 * padded_len<PS>(n + 2) + 8);
-  size_t off = 3 * static_cast<size_t>(p.f.buf_len) * sizeof(A);
-  off = (off + 15) / 16 * 16;
-  p.gw_off = static_cast<int>(off);
-  off += (EPI == EPI_STORE ? 2 : 1) * static_cast<size_t>(p.gw_len) * sizeof(A);
-  off = (off + 15) / 16 * 16;
-  p.tab_off = static_cast<int>(off);
-  size_t tab = 0;  // the largest octave's tap tables
-  for (int j = 0; j < pl->n_octaves; ++j)
-    tab = std::max(tab, 4 * static_cast<size_t>(pl->oct_count[j]) * (pl->oct_half[j] + 1));
-  off += tab * sizeof(A);
-  off = (off + 15) / 16 * 16;
-  p.red_off = static_cast<int>(off);
-  off += NW * sizeof(A);
-  const size_t smem = off + 16;
-  const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
+  const size_t smem = row_bwd_smem<A, EPI>(n, pl, p.f.ext, &p);
   if (smem > budget) return FDWT_ERR_UNSUPPORTED;
   if (!p.need_gx && gh == nullptr && EPI == EPI_STORE) return FDWT_OK;
   auto kern = cwt_backward_kernel<A, EPI>;

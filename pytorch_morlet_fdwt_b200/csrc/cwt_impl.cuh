@@ -2,13 +2,23 @@
 // consumers (magnitude/phase mix, online spectral softmax).  Templates; instantiated per
 // element type in cwt_f32.cu / cwt_f64.cu.
 //
-// One CTA owns one signal row.  The pyramid x_0, x_1, ... lives in two ping-pong shared
-// buffers that cover every position a later octave reads; x_j is exactly the reference's
-// zero-padded, margin-truncated signal (fdwt/cwt.py:130-138, 512-519): it is nonzero only on
-// [-e_j, n + e_j) with e_0 = 0 and e_{j+1} = min(margin_{j+1}, e_j + c_lp 2^j), and is stored as
-// zeros elsewhere.  Octave j applies the Morlet filters of its scales at spacing 2^j
-// (fdwt/kernels/conv.py:38-134) and then the dilated half-band step produces x_{j+1}
-// (fdwt/kernels/conv.py:251-279).
+// One CTA owns one signal row, or one time tile of a row too long for one CTA's shared memory.
+// The pyramid x_0, x_1, ... lives in two ping-pong shared buffers that cover every position a
+// later octave reads; x_j is exactly the reference's zero-padded, margin-truncated signal
+// (fdwt/cwt.py:130-138, 512-519): it is nonzero only on [-e_j, n + e_j) with e_0 = 0 and
+// e_{j+1} = min(margin_{j+1}, e_j + c_lp 2^j), and is stored as zeros elsewhere.
+//
+// Time tiles.  A tile owns the outputs [t0, t0 + tk) and its buffers cover [t0 - H, t0 + tk + H)
+// with H the reach of the pyramid: H_J-1 = half_J-1 2^(J-1), H_j = max(half_j 2^j,
+// H_j+1 + c_lp 2^j), H = H_0.  x_j is then exact on [t0 - H_j, t0 + tk + H_j), which holds
+// every position the tile's outputs of octave j read; positions further out are computed from
+// an incomplete window (or set to zero where the window leaves the buffer) and never read by a
+// kept output.  A whole row is the tile t0 = 0, tk = n with H the row's reach (positions past
+// the live extents are zero).  The PYR mode runs the half-band chain alone over tiles of
+// [-e, n + e) and writes x_1 .. x_J-1 to global memory for the backward pass.
+//
+// Octave j applies the Morlet filters of its scales at spacing 2^j (fdwt/kernels/conv.py:38-134)
+// and then the dilated half-band step produces x_{j+1} (fdwt/kernels/conv.py:251-279).
 //
 // Filter stage.  A work item is P consecutive polyphase outputs n_i = phi + 2^j (u0 + i) of one
 // phase; the thread keeps a left window x[n_i - 2^j k] and a right window x[n_i + 2^j k] in
@@ -43,7 +53,7 @@ constexpr int kMaxOct = FDWT_MAX_OCTAVES;
 constexpr int kMaxScales = FDWT_MAX_SCALES;
 constexpr int kMaxC = (FDWT_MAX_LOWPASS - 1) / 2;
 
-enum Epi { EPI_STORE = 0, EPI_MIX = 1, EPI_SOFTMAX = 2 };
+enum Epi { EPI_STORE = 0, EPI_MIX = 1, EPI_SOFTMAX = 2, EPI_PYR = 3 };
 
 struct Oct {
   int32_t dil, half, begin, count;
@@ -80,6 +90,18 @@ struct FwdParams {
   Oct oct[kMaxOct];
   int32_t order[kMaxScales];
   int32_t support[kMaxScales];
+  // time tiles: CTA b owns [t_base + (b % ntile) t_len, ...) up to t_end, buffers reach `halo`
+  // past both ends of the owned range (a whole row: ntile 1, t_len = t_end = n, halo = ext)
+  int32_t ntile, t_len, t_base, t_end, halo;
+  // PYR: x_j (j >= 1, pyr_off[j] >= 0) into pyr + row * pyr_len + pyr_off[j] on [-live_j, n + live_j)
+  A* pyr;
+  int64_t pyr_len;
+  int32_t pyr_off[kMaxOct];
+};
+
+// The part of a row a CTA computes: buffers cover [org, org + span); kept outputs [t0, tend).
+struct Span {
+  int org, limit, t0, tend;
 };
 
 // ------------------------------------------------------------------------------ helpers
@@ -226,9 +248,10 @@ __device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* fla
 template <typename A, int SB, bool SYM, bool GTAB>
 __device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
                                            const A* __restrict__ xb, int phi, int u0, int limit,
-                                           const A* __restrict__ tab, int s0, int K,
+                                           int org, const A* __restrict__ tab, int s0, int K,
                                            Acc2<A> (&acc)[SB][P]) {
-  const int ext = p.ext, dil = O.dil, cnt = O.count;
+  const int dil = O.dil, cnt = O.count;
+  const int ext = -org;  // buffer index of position q: sidx(q - org)
   A L[P], R[P];
 #pragma unroll
   for (int i = 0; i < P; ++i) {
@@ -286,17 +309,17 @@ __device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
 template <typename T, typename A, int EPI, int SB, bool SYM>
 __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, const A* xb,
                                          const A* tab, int s0, int K, int phi, int u0,
-                                         int64_t row, A (&mix)[P], A (&sm_m)[P], A (&sm_l)[P],
-                                         A (&sm_num)[P]) {
+                                         int64_t row, const Span& sp, A (&mix)[P], A (&sm_m)[P],
+                                         A (&sm_l)[P], A (&sm_num)[P]) {
   const int64_t n = p.n;
+  const int64_t tend = sp.tend;  // outputs past the kept range read clamped windows (limit =
+                                 // the last buffer position) and are not stored
   const int dil = O.dil;
-  const int limit = static_cast<int>(n) + p.ext - 1;  // last buffer position: outputs past
-                                                       // the row end read clamped windows
   Acc2<A> acc[SB][P];
   if (O.count * (O.half + 1) * 4 <= p.coef_cap)
-    conv_block<A, SB, SYM, false>(p, O, xb, phi, u0, limit, tab, s0, K, acc);
+    conv_block<A, SB, SYM, false>(p, O, xb, phi, u0, sp.limit, sp.org, tab, s0, K, acc);
   else
-    conv_block<A, SB, SYM, true>(p, O, xb, phi, u0, limit, tab, s0, K, acc);
+    conv_block<A, SB, SYM, true>(p, O, xb, phi, u0, sp.limit, sp.org, tab, s0, K, acc);
   const int C = p.channels;
 #pragma unroll
   for (int s = 0; s < SB; ++s) {
@@ -304,7 +327,7 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
     if (EPI == EPI_STORE) {
       A* yb = static_cast<A*>(p.y) + ((row * p.n_scales + gs) * n) * C;
       const int64_t n0 = phi + static_cast<int64_t>(dil) * u0;
-      if (C == 2 && dil == 1 && n0 + P <= n &&
+      if (C == 2 && dil == 1 && n0 + P <= tend &&
           (reinterpret_cast<uintptr_t>(yb + 2 * n0) & 15) == 0) {
         // 8 consecutive complex outputs: whole 16-byte vectors
         if constexpr (std::is_same<A, float>::value) {
@@ -322,7 +345,7 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
 #pragma unroll
         for (int i = 0; i < P; ++i) {
           const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
-          if (ni < n) {
+          if (ni < tend) {
             if (C == 2) {
               typename std::conditional<std::is_same<A, float>::value, float2, double2>::type v;
               v.x = acc[s][i].re();
@@ -353,7 +376,7 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
         const A re = acc[s][i].re(), im = acc[s][i].im();
         const A a = sqrt(re * re + im * im) * p.inv_tau;
         A v;
-        if (p.v_pos) v = ni < n ? V[(g * p.n_scales + gs) * n + ni] : A(0);
+        if (p.v_pos) v = ni < tend ? V[(g * p.n_scales + gs) * n + ni] : A(0);
         else v = V[c * p.n_scales + gs];
         const A m_new = fmax(sm_m[i], a);
         const A alpha = exp(sm_m[i] - m_new);
@@ -369,34 +392,38 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
 template <typename T, typename A, int EPI, int SB>
 __device__ __forceinline__ void do_block_sym(const FwdParams<A>& p, const Oct& O, const A* xb,
                                              const A* tab, int s0, int K, bool sym, int phi, int u0,
-                                             int64_t row, A (&mix)[P], A (&sm_m)[P],
-                                             A (&sm_l)[P], A (&sm_num)[P]) {
-  if (sym) do_block<T, A, EPI, SB, true>(p, O, xb, tab, s0, K, phi, u0, row, mix, sm_m, sm_l, sm_num);
-  else do_block<T, A, EPI, SB, false>(p, O, xb, tab, s0, K, phi, u0, row, mix, sm_m, sm_l, sm_num);
+                                             int64_t row, const Span& sp, A (&mix)[P],
+                                             A (&sm_m)[P], A (&sm_l)[P], A (&sm_num)[P]) {
+  if (sym) do_block<T, A, EPI, SB, true>(p, O, xb, tab, s0, K, phi, u0, row, sp, mix, sm_m, sm_l, sm_num);
+  else do_block<T, A, EPI, SB, false>(p, O, xb, tab, s0, K, phi, u0, row, sp, mix, sm_m, sm_l, sm_num);
 }
 
 // Dispatch a block of runtime size 1..4.
 template <typename T, typename A, int EPI>
 __device__ __forceinline__ void run_block(const FwdParams<A>& p, const Oct& O, const A* xb,
                                           const A* tab, int s0, int sb, int K, bool sym,
-                                          int phi, int u0, int64_t row, A (&mix)[P],
-                                          A (&sm_m)[P], A (&sm_l)[P], A (&sm_num)[P]) {
+                                          int phi, int u0, int64_t row, const Span& sp,
+                                          A (&mix)[P], A (&sm_m)[P], A (&sm_l)[P],
+                                          A (&sm_num)[P]) {
   switch (sb) {
-    case 1: do_block_sym<T, A, EPI, 1>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
-    case 2: do_block_sym<T, A, EPI, 2>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
-    case 3: do_block_sym<T, A, EPI, 3>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
-    default: do_block_sym<T, A, EPI, 4>(p, O, xb, tab, s0, K, sym, phi, u0, row, mix, sm_m, sm_l, sm_num); break;
+    case 1: do_block_sym<T, A, EPI, 1>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    case 2: do_block_sym<T, A, EPI, 2>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    case 3: do_block_sym<T, A, EPI, 3>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    default: do_block_sym<T, A, EPI, 4>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
   }
 }
 
-// x_{j+1} from x_j (dilation dil), written over the whole buffer range (zero outside live).
+// x_{j+1} from x_j (dilation dil) over the buffer [org, org + span): zero outside live and where
+// the window leaves the buffer (positions no kept output reads, see the tile notes above).
 template <typename A>
-__device__ void lowpass_step(const FwdParams<A>& p, const A* cur, A* nxt, int dil, int live) {
+__device__ void lowpass_step(const FwdParams<A>& p, const A* cur, A* nxt, int dil, int live,
+                             int org, int span) {
   const int n = static_cast<int>(p.n);
-  const int ext = p.ext;
-  for (int q = threadIdx.x - ext; q < n + ext; q += NT) {
+  const int ext = -org;
+  const int reach = p.n_lp > 0 ? p.lp_t[p.n_lp - 1] * dil : 0;
+  for (int q = static_cast<int>(threadIdx.x) + org; q < org + span; q += NT) {
     A v = A(0);
-    if (q >= -live && q < n + live) {
+    if (q >= -live && q < n + live && q - reach >= org && q + reach < org + span) {
       v = p.lpp[0] * cur[sidx<PS>(q + ext)];
       if (p.lp_sym) {
         for (int i = 0; i < p.n_lp; ++i) {
@@ -426,23 +453,30 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   A* extra = reinterpret_cast<A*>(smem + p.extra_off);
   __shared__ int flags[8];
   __shared__ int kmx[8];  // per scale block: last tap with a nonzero coefficient
-  const int64_t row = blockIdx.x;
+  const int64_t row = blockIdx.x / p.ntile;
+  const int tile = static_cast<int>(blockIdx.x - row * p.ntile);
   const int n = static_cast<int>(p.n);
-  const int ext = p.ext;
   const int tid = threadIdx.x;
+  Span sp;
+  sp.t0 = p.t_base + tile * p.t_len;
+  const int tk = min(p.t_len, p.t_end - sp.t0);  // owned (kept) positions [t0, t0 + tk)
+  sp.tend = sp.t0 + tk;
+  sp.org = sp.t0 - p.halo;
+  const int span = tk + 2 * p.halo;
+  sp.limit = sp.org + span - 1;
 
   const T* xr = static_cast<const T*>(p.x) + row * p.n;
-  for (int i = tid; i < n + 2 * ext; i += NT) {
-    const int q = i - ext;
+  for (int i = tid; i < span; i += NT) {
+    const int q = sp.org + i;
     buf0[sidx<PS>(i)] = (q >= 0 && q < n) ? to_acc<T>(xr[q]) : A(0);
   }
   if (EPI == EPI_MIX) {
-    for (int i = tid; i < n; i += NT) extra[i] = A(0);
+    for (int i = tid; i < tk; i += NT) extra[i] = A(0);
   } else if (EPI == EPI_SOFTMAX) {
-    for (int i = tid; i < n; i += NT) {
+    for (int i = tid; i < tk; i += NT) {
       extra[i] = -INFINITY;
-      extra[n + i] = A(0);
-      extra[2 * n + i] = A(0);
+      extra[tk + i] = A(0);
+      extra[2 * tk + i] = A(0);
     }
   }
   __syncthreads();
@@ -451,11 +485,11 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   A* nxt = buf1;
   for (int j = 0; j < p.n_oct; ++j) {
     const Oct& O = p.oct[j];
-    if (O.count > 0) {
+    if (O.count > 0 && EPI != EPI_PYR) {
       build_coef<A>(p, O, tab, flags, kmx);
       __syncthreads();
       const int dil = O.dil;
-      const int runs = (static_cast<int>((p.n + dil - 1) / dil) + P - 1) / P;
+      const int runs = (static_cast<int>((tk + dil - 1) / dil) + P - 1) / P;
       const int items = dil * runs;
       int nblk = 0;
       for (int s0 = 0; s0 < O.count; s0 += block_size(O.count - s0)) ++nblk;
@@ -466,25 +500,24 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
           int s0 = 0;
           for (int b = 0; b < blk; ++b) s0 += block_size(O.count - s0);
           const int phi = it % dil, u0 = (it / dil) * P;
-          if (phi >= n) continue;
+          if (phi >= tk) continue;
           A mix[P], m_[P], l_[P], num_[P];
           run_block<T, A, EPI>(p, O, cur, tab, s0, block_size(O.count - s0), kmx[blk],
-                               flags[blk] == 0,
-                               phi, u0, row, mix, m_, l_, num_);
+                               flags[blk] == 0, sp.t0 + phi, u0, row, sp, mix, m_, l_, num_);
         }
       } else {
         for (int it = tid; it < items; it += NT) {
           const int phi = it % dil, u0 = (it / dil) * P;
-          if (phi >= n) continue;
+          if (phi >= tk) continue;
           A mix[P], sm_m[P], sm_l[P], sm_num[P];
 #pragma unroll
           for (int i = 0; i < P; ++i) {
-            const int ni = phi + dil * (u0 + i);
+            const int li = phi + dil * (u0 + i);  // tile-local output index
             mix[i] = A(0);
-            if (EPI == EPI_SOFTMAX && ni < n) {
-              sm_m[i] = extra[ni];
-              sm_l[i] = extra[n + ni];
-              sm_num[i] = extra[2 * n + ni];
+            if (EPI == EPI_SOFTMAX && li < tk) {
+              sm_m[i] = extra[li];
+              sm_l[i] = extra[tk + li];
+              sm_num[i] = extra[2 * tk + li];
             } else {
               sm_m[i] = -INFINITY;
               sm_l[i] = A(0);
@@ -496,20 +529,20 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
             const int sb = block_size(O.count - s0);
             // (the fused epilogues keep the octave's full tap range: the per-block limit made
             // the mix and softmax kernels slower on B200, 2.04 -> 2.50 ms on cfg4)
-            run_block<T, A, EPI>(p, O, cur, tab, s0, sb, O.half, flags[b] == 0, phi, u0, row, mix,
-                                 sm_m, sm_l, sm_num);
+            run_block<T, A, EPI>(p, O, cur, tab, s0, sb, O.half, flags[b] == 0, sp.t0 + phi, u0,
+                                 row, sp, mix, sm_m, sm_l, sm_num);
             s0 += sb;
           }
 #pragma unroll
           for (int i = 0; i < P; ++i) {
-            const int ni = phi + dil * (u0 + i);
-            if (ni < n) {
+            const int li = phi + dil * (u0 + i);
+            if (li < tk) {
               if (EPI == EPI_MIX) {
-                extra[ni] += mix[i];
+                extra[li] += mix[i];
               } else {
-                extra[ni] = sm_m[i];
-                extra[n + ni] = sm_l[i];
-                extra[2 * n + ni] = sm_num[i];
+                extra[li] = sm_m[i];
+                extra[tk + li] = sm_l[i];
+                extra[2 * tk + li] = sm_num[i];
               }
             }
           }
@@ -518,8 +551,15 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
       __syncthreads();
     }
     if (j + 1 < p.n_oct) {
-      lowpass_step<A>(p, cur, nxt, O.dil, p.oct[j + 1].live);
+      lowpass_step<A>(p, cur, nxt, O.dil, p.oct[j + 1].live, sp.org, span);
       __syncthreads();
+      if (EPI == EPI_PYR && p.pyr_off[j + 1] >= 0) {
+        // x_{j+1} on the owned positions inside its live extent
+        const int lv = p.oct[j + 1].live;
+        A* dst = p.pyr + row * p.pyr_len + p.pyr_off[j + 1] + lv;
+        const int lo = max(sp.t0, -lv), hi = min(sp.tend, n + lv);
+        for (int q = lo + tid; q < hi; q += NT) dst[q] = nxt[sidx<PS>(q - sp.org)];
+      }
       A* t = cur;
       cur = nxt;
       nxt = t;
@@ -527,15 +567,15 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   }
 
   if (EPI == EPI_MIX) {
-    A* yr = static_cast<A*>(p.y) + row * p.n;
-    for (int i = tid; i < n; i += NT) yr[i] = extra[i];
+    A* yr = static_cast<A*>(p.y) + row * p.n + sp.t0;
+    for (int i = tid; i < tk; i += NT) yr[i] = extra[i];
   } else if (EPI == EPI_SOFTMAX) {
-    A* o = static_cast<A*>(p.y) + row * p.n;
-    A* mo = static_cast<A*>(p.m_out) + row * p.n;
-    A* lo = static_cast<A*>(p.l_out) + row * p.n;
-    for (int i = tid; i < n; i += NT) {
-      const A l = extra[n + i];
-      o[i] = extra[2 * n + i] / l;
+    A* o = static_cast<A*>(p.y) + row * p.n + sp.t0;
+    A* mo = static_cast<A*>(p.m_out) + row * p.n + sp.t0;
+    A* lo = static_cast<A*>(p.l_out) + row * p.n + sp.t0;
+    for (int i = tid; i < tk; i += NT) {
+      const A l = extra[tk + i];
+      o[i] = extra[2 * tk + i] / l;
       mo[i] = extra[i];
       lo[i] = l;
     }
@@ -631,6 +671,92 @@ void fill_common(FwdParams<A>& p, const fdwt_morlet_plan* pl, const Geometry& g,
   }
 }
 
+// Reach of a tile's pyramid buffers past both ends of its owned range (the H of the tile
+// notes): the filter reach of each octave and the half-band chain below it.  pyr_only: the
+// half-band chain alone (x_1 .. x_J-1 on the owned range).
+inline int tile_halo(const fdwt_morlet_plan* pl, bool pyr_only) {
+  int H = 0;
+  for (int j = pl->n_octaves - 1; j >= 0; --j) {
+    const int dil = 1 << j;
+    const int own = (!pyr_only && pl->oct_count[j] > 0) ? pl->oct_half[j] * dil : 0;
+    const int chain = j + 1 < pl->n_octaves ? H + pl->c_lp * dil : 0;
+    H = std::max(own, chain);
+  }
+  return H + 8;
+}
+
+// Shared-memory layout of a forward launch whose CTAs own t_len positions and whose buffers
+// reach `halo` past both ends: fills the offsets of p, returns the bytes (0: does not fit).
+template <typename A, int EPI>
+size_t fwd_layout(FwdParams<A>& p, const fdwt_morlet_plan* pl, int64_t t_len, int halo,
+                  size_t budget) {
+  const int64_t span = t_len + 2 * static_cast<int64_t>(halo);
+  if (span > 0x3fffffffLL) return 0;
+  p.buf_len = static_cast<int>(padded_len<PS>(span) + 8);
+  // the coefficient table takes what is left of the shared budget (up to the largest octave)
+  int coef = 0;
+  if (EPI != EPI_PYR)
+    for (int j = 0; j < pl->n_octaves; ++j)
+      coef = std::max(coef, pl->oct_count[j] * (pl->oct_half[j] + 1) * 4);
+  const size_t nextra = (EPI == EPI_MIX ? 1 : EPI == EPI_SOFTMAX ? 3 : 0) *
+                        static_cast<size_t>(t_len);
+  const size_t fixed = 2 * static_cast<size_t>(p.buf_len) * sizeof(A) + 64 + nextra * sizeof(A);
+  if (fixed > budget) return 0;
+  const size_t room = (budget - fixed) / sizeof(A);
+  if (static_cast<size_t>(coef) > room) coef = static_cast<int>(room / 4 * 4);
+  coef = std::min(coef, 24 * 1024 / static_cast<int>(sizeof(A)) * 4);  // keep occupancy
+  p.coef_cap = coef;
+  size_t off = 2 * static_cast<size_t>(p.buf_len) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  p.coef_off = static_cast<int>(off);
+  off += static_cast<size_t>(coef) * sizeof(A);
+  off = (off + 15) / 16 * 16;
+  p.extra_off = static_cast<int>(off);
+  off += nextra * sizeof(A);
+  const size_t smem = off + 16;
+  return smem > budget ? 0 : smem;
+}
+
+// Tiles of the range [t_base, t_end) for a forward launch: the longest tile (a power of two,
+// at least 256) whose layout keeps two CTAs per SM, else the longest that fits at all; a test
+// may force the tile length (fdwt_set_cwt_tile_test).  Returns the shared bytes (0: none fits).
+template <typename A, int EPI>
+size_t plan_fwd_tiles(FwdParams<A>& p, const fdwt_morlet_plan* pl, int64_t t_base,
+                      int64_t t_end, int halo, size_t budget) {
+  const int64_t range = t_end - t_base;
+  p.t_base = static_cast<int32_t>(t_base);
+  p.t_end = static_cast<int32_t>(t_end);
+  p.halo = halo;
+  auto take = [&](int64_t tl) -> size_t {
+    const size_t sm = fwd_layout<A, EPI>(p, pl, tl, halo, budget);
+    if (sm) {
+      p.t_len = static_cast<int32_t>(tl);
+      p.ntile = static_cast<int32_t>(cdiv(range, tl));
+    }
+    return sm;
+  };
+  const int forced = cwt_tile_test();
+  if (forced > 0) return take(std::min<int64_t>(forced, range));
+  const size_t two_per_sm = std::min(budget, static_cast<size_t>(113) << 10);
+  for (const size_t cap : {two_per_sm, budget})
+    for (int64_t tl = int64_t(1) << 16; tl >= 256; tl >>= 1) {
+      const size_t sm = fwd_layout<A, EPI>(p, pl, std::min(tl, range), halo, cap);
+      if (sm) return take(std::min(tl, range));
+    }
+  return 0;
+}
+
+template <typename T, typename A, int EPI>
+int launch_forward(FwdParams<A>& p, int64_t rows, size_t smem, cudaStream_t stream) {
+  if (rows * p.ntile > 0x7fffffffLL) return FDWT_ERR_UNSUPPORTED;
+  auto kern = cwt_forward_kernel<T, A, EPI>;
+  int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
+  if (st != FDWT_OK) return st;
+  if ((st = pre_launch(stream)) != FDWT_OK) return st;
+  kern<<<static_cast<unsigned>(rows * p.ntile), NT, smem, stream>>>(p);
+  return launch_status();
+}
+
 template <typename T, typename A, int EPI>
 int run_forward(int64_t rows, int64_t n, const void* x, const void* h,
                 const fdwt_morlet_plan* pl, void* y, const void* a, const void* b,
@@ -654,36 +780,45 @@ int run_forward(int64_t rows, int64_t n, const void* x, const void* h,
   p.dim = dim;
   p.v_pos = v_pos;
   p.inv_tau = static_cast<A>(inv_tau);
-  const int64_t span = n + 2 * static_cast<int64_t>(g.ext);
-  p.buf_len = static_cast<int>(padded_len<PS>(span) + 8);
-  // the coefficient table takes what is left of the shared budget (up to the largest octave)
-  int coef = 0;
-  for (int j = 0; j < pl->n_octaves; ++j)
-    coef = std::max(coef, pl->oct_count[j] * (pl->oct_half[j] + 1) * 4);
   const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
-  const size_t fixed = 2 * static_cast<size_t>(p.buf_len) * sizeof(A) + 64 +
-      (EPI == EPI_MIX ? 1 : EPI == EPI_SOFTMAX ? 3 : 0) * static_cast<size_t>(n) * sizeof(A);
-  if (fixed > budget) return FDWT_ERR_UNSUPPORTED;
-  const size_t room = (budget - fixed) / sizeof(A);
-  if (static_cast<size_t>(coef) > room) coef = static_cast<int>(room / 4 * 4);
-  coef = std::min(coef, 24 * 1024 / static_cast<int>(sizeof(A)) * 4);  // keep occupancy
-  p.coef_cap = coef;
-  size_t off = 2 * static_cast<size_t>(p.buf_len) * sizeof(A);
-  off = (off + 15) / 16 * 16;
-  p.coef_off = static_cast<int>(off);
-  off += static_cast<size_t>(coef) * sizeof(A);
-  off = (off + 15) / 16 * 16;
-  p.extra_off = static_cast<int>(off);
-  if (EPI == EPI_MIX) off += static_cast<size_t>(n) * sizeof(A);
-  if (EPI == EPI_SOFTMAX) off += 3 * static_cast<size_t>(n) * sizeof(A);
-  const size_t smem = off + 16;
-  if (smem > budget) return FDWT_ERR_UNSUPPORTED;
-  auto kern = cwt_forward_kernel<T, A, EPI>;
-  st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
-  if (st != FDWT_OK) return st;
-  if ((st = pre_launch(stream)) != FDWT_OK) return st;
-  kern<<<static_cast<unsigned>(rows), NT, smem, stream>>>(p);
-  return launch_status();
+  // a whole row per CTA when it fits (buffers over the row's own reach); time tiles otherwise
+  size_t smem = 0;
+  if (cwt_tile_test() <= 0) {
+    smem = fwd_layout<A, EPI>(p, pl, n, g.ext, budget);
+    if (smem) {
+      p.ntile = 1;
+      p.t_len = static_cast<int32_t>(n);
+      p.t_base = 0;
+      p.t_end = static_cast<int32_t>(n);
+      p.halo = g.ext;
+    }
+  }
+  if (!smem) smem = plan_fwd_tiles<A, EPI>(p, pl, 0, n, tile_halo(pl, false), budget);
+  if (!smem) return FDWT_ERR_UNSUPPORTED;
+  return launch_forward<T, A, EPI>(p, rows, smem, stream);
+}
+
+// x_1 .. x_J-1 of every row into pyr (row stride pyr_len; level j at pyr_off[j] >= 0, stored on
+// [-live_j, n + live_j)): the half-band chain of the forward over tiles of [-e, n + e), e the
+// largest live extent.
+template <typename A>
+int run_pyramid(int64_t rows, int64_t n, const void* x, const fdwt_morlet_plan* pl,
+                const Geometry& g, A* pyr, int64_t pyr_len, const int32_t* pyr_off,
+                cudaStream_t stream) {
+  if (rows == 0 || pl->n_octaves < 2) return FDWT_OK;
+  FwdParams<A> p{};
+  fill_common(p, pl, g, n);
+  p.rows = rows;
+  p.x = x;
+  p.pyr = pyr;
+  p.pyr_len = pyr_len;
+  for (int j = 0; j < kMaxOct; ++j) p.pyr_off[j] = pyr_off[j];
+  int e = 0;
+  for (int j = 0; j < pl->n_octaves; ++j) e = std::max(e, g.live[j]);
+  const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
+  const size_t smem = plan_fwd_tiles<A, EPI_PYR>(p, pl, -e, n + e, tile_halo(pl, true), budget);
+  if (!smem) return FDWT_ERR_UNSUPPORTED;
+  return launch_forward<A, A, EPI_PYR>(p, rows, smem, stream);
 }
 
 }  // namespace cwtk

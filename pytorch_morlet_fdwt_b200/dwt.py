@@ -106,6 +106,24 @@ def _spec_arrays(spec: _Spec):
             _lib.f64_array(spec.h1), _lib.i64_array(spec.in_len))
 
 
+@functools.lru_cache(maxsize=1024)
+def _analysis_ws(spec: _Spec, rows: int, dt: int, device_index: int) -> int:
+    """Workspace bytes of an analysis call (a pure function of its sizes on one device: the
+    query plans the launches, which costs host time worth saving on every call)."""
+    coef, pad, _, _, _ = _spec_arrays(spec)
+    return int(_lib.load().fdwt_dwt_analysis_workspace(dt, rows, spec.n, spec.levels, coef, pad,
+                                                        len(spec.h0), spec.mode, spec.off))
+
+
+@functools.lru_cache(maxsize=1024)
+def _synthesis_ws(spec: _Spec, rows: int, dt: int, device_index: int) -> int:
+    """Workspace bytes of a synthesis call (see _analysis_ws)."""
+    coef, _, _, _, outl = _spec_arrays(spec)
+    return int(_lib.load().fdwt_dwt_synthesis_workspace(dt, rows, spec.levels, spec.approx_len,
+                                                         coef, outl, len(spec.h0), spec.mode,
+                                                         spec.off))
+
+
 def _rows(t: torch.Tensor, n: int) -> torch.Tensor:
     return t.reshape(-1, n).contiguous()
 
@@ -123,8 +141,7 @@ def _analysis(x: torch.Tensor, spec: _Spec) -> List[torch.Tensor]:
     coef, pad, h0, h1, _ = _spec_arrays(spec)
     dt = _lib.dtype_code(x.dtype)
     with torch.cuda.device(dev):
-        nws = lib.fdwt_dwt_analysis_workspace(dt, R, spec.n, J, coef, pad, L, spec.mode,
-                                               spec.off)
+        nws = _analysis_ws(spec, R, dt, dev.index)
         ws = _lib.workspace(nws, dev)
         st = lib.fdwt_dwt_analysis(
             dt, R, x2.data_ptr(), spec.n, J, coef, pad, _lib.ptr_array(outs),
@@ -155,8 +172,7 @@ def _synthesis(inputs: Sequence[Optional[torch.Tensor]], spec: _Spec) -> torch.T
     coef, _, h0, h1, outl = _spec_arrays(spec)
     dt = _lib.dtype_code(dtype)
     with torch.cuda.device(dev):
-        nws = lib.fdwt_dwt_synthesis_workspace(dt, R, J, spec.approx_len, coef, outl, L,
-                                                spec.mode, spec.off)
+        nws = _synthesis_ws(spec, R, dt, dev.index)
         ws = _lib.workspace(nws, dev)
         st = lib.fdwt_dwt_synthesis(
             dt, R, J, _lib.ptr_array(rows), spec.approx_len, coef, outl, y.data_ptr(),
