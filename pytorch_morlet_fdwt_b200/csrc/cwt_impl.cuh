@@ -20,9 +20,14 @@
 // Octave j applies the Morlet filters of its scales at spacing 2^j (fdwt/kernels/conv.py:38-134)
 // and then the dilated half-band step produces x_{j+1} (fdwt/kernels/conv.py:251-279).
 //
-// Filter stage.  A work item is P consecutive polyphase outputs n_i = phi + 2^j (u0 + i) of one
-// phase; the thread keeps a left window x[n_i - 2^j k] and a right window x[n_i + 2^j k] in
-// registers, each advancing with one shared load per tap.  The Morlet filters are even (real
+// Filter stage.  A work item is PF = 5 consecutive polyphase outputs n_i = phi + 2^j (u0 + i) of
+// one phase; the thread keeps a left window x[n_i - 2^j k] and a right window x[n_i + 2^j k] in
+// registers, each advancing with one shared load per tap through a pointer that moves by 2^j
+// (the pyramid buffers are linear; the lanes of a warp start their windows 5 2^j apart, on
+// distinct banks for every power-of-two 2^j, so no padding is needed).  Items whose windows stay
+// inside the buffer skip the per-load clamp.  A block of up to 5 scales shares the window sums;
+// the scales (sorted by support) leave the tap loop one by one at their own last nonzero tap,
+// so the packed FMAs are exactly the filters' nonzero taps.  The Morlet filters are even (real
 // part) and odd (imaginary part) in k (fdwt/cwt.py:192-203), so a tap pair costs one packed
 // fp32 FMA per scale: (re, im) += (h_re[k], h_im[k]) * (x_l + x_r, x_l - x_r).  The symmetric
 // and antisymmetric halves of every filter are separated exactly when its coefficient table is
@@ -47,7 +52,11 @@ namespace fdwt {
 namespace cwtk {
 
 constexpr int NT = 256;           // threads per CTA
-constexpr int P = 8;              // consecutive polyphase outputs per work item
+constexpr int P = 8;              // consecutive polyphase outputs per work item (backward)
+constexpr int PF = 5;             // the same in the forward: an odd run length keeps the
+                                  // windows of a warp's lanes on distinct banks of the linear
+                                  // (unpadded) buffers for every power-of-two dilation
+constexpr int SBMAX = 5;          // scales per block of the forward's tap loop
 constexpr int PS = 3;             // pyramid buffers: one pad element per 8
 constexpr int kMaxOct = FDWT_MAX_OCTAVES;
 constexpr int kMaxScales = FDWT_MAX_SCALES;
@@ -158,9 +167,9 @@ struct Acc2<double> {
 // Partition of an octave's `count` scales into blocks of 1..4 (each block shares the pair
 // sums of its tap loop).
 __device__ __forceinline__ int block_size(int rem) {
-  if (rem <= 4) return rem;
-  if (rem == 5 || rem == 6 || rem == 9) return 3;
-  return 4;
+  if (rem <= SBMAX) return rem;
+  if (rem <= 2 * SBMAX) return (rem + 1) / 2;
+  return SBMAX;
 }
 
 // Coefficient table of an octave, per tap k in [0, half] and scale slot s:
@@ -170,10 +179,10 @@ __device__ __forceinline__ int block_size(int rem) {
 //   [3] sym(im)  = (h_im[c+k] + h_im[c-k]) / 2   (k = 0: h_im[c])
 // so that  re += [0] (xl + xr) + [2] (xl - xr),  im += [1] (xl - xr) + [3] (xl + xr)  exactly
 // reproduces sum_k h[c+k] x[n - dk] over k = -half..half of the octave.
-// build_coef returns (through flags[]) whether each block has nonzero [2]/[3] halves, and
-// (through kmx[]) the last tap k of each block with a nonzero coefficient: the taps past it are
-// zero for every scale of the block (a scale's filter is shorter than the octave's widest), so
-// the STORE epilogue's tap loop stops there -- exact for any filter tensor.
+// build_coef records per scale slot s whether its [2]/[3] halves are nonzero (anti[s]) and the
+// last tap k with a nonzero coefficient (klast[s]): the taps past it are zero (a scale's filter
+// is shorter than the octave's widest), so the scale leaves the tap loop there -- exact for any
+// filter tensor.
 // fold_coef: folded coefficients of tap k of scale slot s, straight from the filter tensor.
 template <typename A>
 __device__ __forceinline__ void fold_coef(const FwdParams<A>& p, const Oct& O, int s, int k,
@@ -207,15 +216,12 @@ __device__ __forceinline__ void fold_coef(const FwdParams<A>& p, const Oct& O, i
 }
 
 template <typename A>
-__device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* flags, int* kmx) {
-  const A* H = static_cast<const A*>(p.h);
-  const int C = p.channels;
-  const int hcols = 2 * p.center + 1;
+__device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* anti, int* klast) {
   const int cnt = O.count, K = O.half;
   const int tid = threadIdx.x;
-  if (tid < 8) {
-    flags[tid] = 0;
-    kmx[tid] = 0;
+  for (int s = tid; s < cnt; s += NT) {
+    anti[s] = 0;
+    klast[s] = 0;
   }
   __syncthreads();
   const bool in_smem = cnt * (K + 1) * 4 <= p.coef_cap;
@@ -230,74 +236,66 @@ __device__ void build_coef(const FwdParams<A>& p, const Oct& O, A* tab, int* fla
       d[2] = t[2];
       d[3] = t[3];
     }
-    const bool anti = t[2] != A(0) || t[3] != A(0);
-    if (anti || t[0] != A(0) || t[1] != A(0)) {
-      int b = 0, s0 = 0;  // which block holds slot s
-      while (s0 + block_size(cnt - s0) <= s) {
-        s0 += block_size(cnt - s0);
-        ++b;
-      }
-      if (anti) atomicOr(&flags[b], 1);
-      if (k > 0) atomicMax(&kmx[b], k);
-    }
+    const bool an = t[2] != A(0) || t[3] != A(0);
+    if (an) atomicOr(&anti[s], 1);
+    if (k > 0 && (an || t[0] != A(0) || t[1] != A(0))) atomicMax(&klast[s], k);
   }
 }
 
-// (re, im) of the SB scales of a block for the item's P outputs.  Coefficients come from the
-// shared table (GTAB = false) or are folded from the global filter tensor per tap (GTAB).
-template <typename A, int SB, bool SYM, bool GTAB>
-__device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
-                                           const A* __restrict__ xb, int phi, int u0, int limit,
-                                           int org, const A* __restrict__ tab, int s0, int K,
-                                           Acc2<A> (&acc)[SB][P]) {
+// The window state of an item's tap loop: the two register windows, the next load pointers
+// (or index, when clamped) and the block's coefficients of the current tap.
+template <typename A>
+struct TapState {
+  A L[PF], R[PF];
+  const A* pl;
+  const A* pr;
+  int qr;
+  const A* tk;
+  int k;
+};
+
+// Taps state.k .. kend for the scales M .. SB-1 of the block (the earlier ones have left).
+template <typename A, int SB, int M, bool SYM, bool GTAB, bool CLAMP>
+__device__ __forceinline__ void conv_seg(const FwdParams<A>& p, const Oct& O,
+                                         const A* __restrict__ xb, int lim, int s0, int kend,
+                                         TapState<A>& st, Acc2<A> (&acc)[SB][PF]) {
   const int dil = O.dil, cnt = O.count;
-  const int ext = -org;  // buffer index of position q: sidx(q - org)
-  A L[P], R[P];
+#pragma unroll 5
+  for (; st.k <= kend; ++st.k) {
+    st.tk += 4 * cnt;
 #pragma unroll
-  for (int i = 0; i < P; ++i) {
-    const int pos = min(phi + dil * (u0 + i), limit);
-    L[i] = R[i] = xb[sidx<PS>(pos + ext)];
-  }
-  auto coef = [&](int k, int s, A (&t)[4]) {
-    if (GTAB) {
-      fold_coef<A>(p, O, s0 + s, k, t);
+    for (int i = PF - 1; i > 0; --i) st.L[i] = st.L[i - 1];
+#pragma unroll
+    for (int i = 0; i < PF - 1; ++i) st.R[i] = st.R[i + 1];
+    st.L[0] = *st.pl;
+    st.pl -= dil;
+    if (CLAMP) {
+      st.R[PF - 1] = xb[min(st.qr, lim)];
+      st.qr += dil;
     } else {
-      const A* c = tab + (k * cnt + s0 + s) * 4;
-      t[0] = c[0];
-      t[1] = c[1];
-      t[2] = c[2];
-      t[3] = c[3];
+      st.R[PF - 1] = *st.pr;
+      st.pr += dil;
     }
-  };
-#pragma unroll
-  for (int s = 0; s < SB; ++s) {
-    alignas(16) A t[4];
-    coef(0, s, t);
-#pragma unroll
-    for (int i = 0; i < P; ++i) {
-      acc[s][i].zero();
-      acc[s][i].fma(t, L[i], A(0));        // re += h_re[c] x
-      acc[s][i].fma(t + 2, A(0), L[i]);    // im += h_im[c] x
-    }
-  }
-  int pl = phi + dil * (u0 - 1);          // next left load position
-  int pr = phi + dil * (u0 + P);          // next right load position
-#pragma unroll 8
-  for (int k = 1; k <= K; ++k, pl -= dil, pr += dil) {
-#pragma unroll
-    for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
-#pragma unroll
-    for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
-    L[0] = xb[sidx<PS>(pl + ext)];
-    R[P - 1] = xb[sidx<PS>(min(pr, limit) + ext)];
     alignas(16) A t[SB][4];
 #pragma unroll
-    for (int s = 0; s < SB; ++s) coef(k, s, t[s]);
+    for (int s = M; s < SB; ++s) {
+      if (GTAB) {
+        fold_coef<A>(p, O, s0 + s, st.k, t[s]);
+      } else {
+        const A* c = st.tk + 4 * s;
+        t[s][0] = c[0];
+        t[s][1] = c[1];
+        if (!SYM) {
+          t[s][2] = c[2];
+          t[s][3] = c[3];
+        }
+      }
+    }
 #pragma unroll
-    for (int i = 0; i < P; ++i) {
-      const A sum = L[i] + R[i], dif = L[i] - R[i];
+    for (int i = 0; i < PF; ++i) {
+      const A sum = st.L[i] + st.R[i], dif = st.L[i] - st.R[i];
 #pragma unroll
-      for (int s = 0; s < SB; ++s) {
+      for (int s = M; s < SB; ++s) {
         acc[s][i].fma(t[s], sum, dif);
         if (!SYM) acc[s][i].fma(t[s] + 2, dif, sum);
       }
@@ -305,45 +303,90 @@ __device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
   }
 }
 
+// The segments of a block: scale m is the first active one on the taps past the prefix maximum
+// of the earlier scales' last taps, up to its own (prefix maximum) last tap.
+template <typename A, int SB, int M, bool SYM, bool GTAB, bool CLAMP>
+__device__ __forceinline__ void conv_segs(const FwdParams<A>& p, const Oct& O,
+                                          const A* __restrict__ xb, int lim, int s0,
+                                          const int* klast, int e, TapState<A>& st,
+                                          Acc2<A> (&acc)[SB][PF]) {
+  if constexpr (M < SB) {
+    e = max(e, klast[s0 + M]);
+    conv_seg<A, SB, M, SYM, GTAB, CLAMP>(p, O, xb, lim, s0, e, st, acc);
+    conv_segs<A, SB, M + 1, SYM, GTAB, CLAMP>(p, O, xb, lim, s0, klast, e, st, acc);
+  }
+}
+
+// (re, im) of the SB scales of a block for the item's PF outputs.  Coefficients come from the
+// shared table (GTAB = false) or are folded from the global filter tensor per tap (GTAB).
+// CLAMP: some right-window position passes the buffer's last index (items past the kept range).
+template <typename A, int SB, bool SYM, bool GTAB, bool CLAMP>
+__device__ __forceinline__ void conv_block(const FwdParams<A>& p, const Oct& O,
+                                           const A* __restrict__ xb, int phi, int u0, int limit,
+                                           int org, const A* __restrict__ tab, int s0,
+                                           const int* klast, Acc2<A> (&acc)[SB][PF]) {
+  const int dil = O.dil;
+  const int c0 = phi + dil * u0 - org;  // buffer index of the item's first output
+  const int lim = limit - org;          // last buffer index
+  TapState<A> st;
+#pragma unroll
+  for (int i = 0; i < PF; ++i) {
+    const int q = CLAMP ? min(c0 + dil * i, lim) : c0 + dil * i;
+    st.L[i] = st.R[i] = xb[q];
+  }
+  st.tk = tab + 4 * s0;  // the block's coefficients of tap 0
+#pragma unroll
+  for (int s = 0; s < SB; ++s) {
+    alignas(16) A t[4];
+    if (GTAB) {
+      fold_coef<A>(p, O, s0 + s, 0, t);
+    } else {
+      const A* c = st.tk + 4 * s;
+      t[0] = c[0];
+      t[1] = c[1];
+      t[2] = c[2];
+      t[3] = c[3];
+    }
+#pragma unroll
+    for (int i = 0; i < PF; ++i) {
+      acc[s][i].zero();
+      acc[s][i].fma(t, st.L[i], A(0));        // re += h_re[c] x
+      acc[s][i].fma(t + 2, A(0), st.L[i]);    // im += h_im[c] x
+    }
+  }
+  st.pl = xb + (c0 - dil);         // next left load
+  st.pr = xb + (c0 + dil * PF);    // next right load (no clamp)
+  st.qr = c0 + dil * PF;           // next right load index (clamp)
+  st.k = 1;
+  conv_segs<A, SB, 0, SYM, GTAB, CLAMP>(p, O, xb, lim, s0, klast, 0, st, acc);
+}
+
 // One block for one item, then its epilogue.
-template <typename T, typename A, int EPI, int SB, bool SYM>
+template <typename T, typename A, int EPI, bool GT, int SB, bool SYM>
 __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, const A* xb,
-                                         const A* tab, int s0, int K, int phi, int u0,
-                                         int64_t row, const Span& sp, A (&mix)[P], A (&sm_m)[P],
-                                         A (&sm_l)[P], A (&sm_num)[P]) {
+                                         const A* tab, int s0, const int* klast, int phi, int u0,
+                                         int64_t row, const Span& sp, A (&mix)[PF], A (&sm_m)[PF],
+                                         A (&sm_l)[PF], A (&sm_num)[PF]) {
   const int64_t n = p.n;
   const int64_t tend = sp.tend;  // outputs past the kept range read clamped windows (limit =
                                  // the last buffer position) and are not stored
   const int dil = O.dil;
-  Acc2<A> acc[SB][P];
-  if (O.count * (O.half + 1) * 4 <= p.coef_cap)
-    conv_block<A, SB, SYM, false>(p, O, xb, phi, u0, sp.limit, sp.org, tab, s0, K, acc);
-  else
-    conv_block<A, SB, SYM, true>(p, O, xb, phi, u0, sp.limit, sp.org, tab, s0, K, acc);
+  Acc2<A> acc[SB][PF];
+  int K = 0;  // the block's last nonzero tap
+#pragma unroll
+  for (int s = 0; s < SB; ++s) K = max(K, klast[s0 + s]);
+  const bool clamp = phi + dil * (u0 + PF - 1 + K) > sp.limit;
+  if (clamp) conv_block<A, SB, SYM, GT, true>(p, O, xb, phi, u0, sp.limit, sp.org, tab, s0, klast, acc);
+  else conv_block<A, SB, SYM, GT, false>(p, O, xb, phi, u0, sp.limit, sp.org, tab, s0, klast, acc);
   const int C = p.channels;
 #pragma unroll
   for (int s = 0; s < SB; ++s) {
     const int gs = p.order[O.begin + s0 + s];
     if (EPI == EPI_STORE) {
       A* yb = static_cast<A*>(p.y) + ((row * p.n_scales + gs) * n) * C;
-      const int64_t n0 = phi + static_cast<int64_t>(dil) * u0;
-      if (C == 2 && dil == 1 && n0 + P <= tend &&
-          (reinterpret_cast<uintptr_t>(yb + 2 * n0) & 15) == 0) {
-        // 8 consecutive complex outputs: whole 16-byte vectors
-        if constexpr (std::is_same<A, float>::value) {
-          float4* d = reinterpret_cast<float4*>(yb + 2 * n0);
+      {
 #pragma unroll
-          for (int i = 0; i < P; i += 2)
-            d[i / 2] = make_float4(acc[s][i].re(), acc[s][i].im(), acc[s][i + 1].re(),
-                                   acc[s][i + 1].im());
-        } else {
-          double2* d = reinterpret_cast<double2*>(yb + 2 * n0);
-#pragma unroll
-          for (int i = 0; i < P; ++i) d[i] = make_double2(acc[s][i].re(), acc[s][i].im());
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < P; ++i) {
+        for (int i = 0; i < PF; ++i) {
           const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
           if (ni < tend) {
             if (C == 2) {
@@ -362,7 +405,7 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
       const A av = static_cast<const A*>(p.a)[d * p.n_scales + gs];
       const A bv = static_cast<const A*>(p.b)[d * p.n_scales + gs];
 #pragma unroll
-      for (int i = 0; i < P; ++i) {
+      for (int i = 0; i < PF; ++i) {
         const A re = acc[s][i].re(), im = acc[s][i].im();
         const A mag = C == 2 ? sqrt(re * re + im * im) : fabs(re);
         mix[i] += av * mag + bv * re;
@@ -371,7 +414,7 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
       const A* V = static_cast<const A*>(p.a);
       const int64_t g = row / p.dim, c = row % p.dim;
 #pragma unroll
-      for (int i = 0; i < P; ++i) {
+      for (int i = 0; i < PF; ++i) {
         const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
         const A re = acc[s][i].re(), im = acc[s][i].im();
         const A a = sqrt(re * re + im * im) * p.inv_tau;
@@ -389,27 +432,28 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
   }
 }
 
-template <typename T, typename A, int EPI, int SB>
+template <typename T, typename A, int EPI, bool GT, int SB>
 __device__ __forceinline__ void do_block_sym(const FwdParams<A>& p, const Oct& O, const A* xb,
-                                             const A* tab, int s0, int K, bool sym, int phi, int u0,
-                                             int64_t row, const Span& sp, A (&mix)[P],
-                                             A (&sm_m)[P], A (&sm_l)[P], A (&sm_num)[P]) {
-  if (sym) do_block<T, A, EPI, SB, true>(p, O, xb, tab, s0, K, phi, u0, row, sp, mix, sm_m, sm_l, sm_num);
-  else do_block<T, A, EPI, SB, false>(p, O, xb, tab, s0, K, phi, u0, row, sp, mix, sm_m, sm_l, sm_num);
+                                             const A* tab, int s0, const int* K, bool sym, int phi, int u0,
+                                             int64_t row, const Span& sp, A (&mix)[PF],
+                                             A (&sm_m)[PF], A (&sm_l)[PF], A (&sm_num)[PF]) {
+  if (sym) do_block<T, A, EPI, GT, SB, true>(p, O, xb, tab, s0, K, phi, u0, row, sp, mix, sm_m, sm_l, sm_num);
+  else do_block<T, A, EPI, GT, SB, false>(p, O, xb, tab, s0, K, phi, u0, row, sp, mix, sm_m, sm_l, sm_num);
 }
 
 // Dispatch a block of runtime size 1..4.
-template <typename T, typename A, int EPI>
+template <typename T, typename A, int EPI, bool GT>
 __device__ __forceinline__ void run_block(const FwdParams<A>& p, const Oct& O, const A* xb,
-                                          const A* tab, int s0, int sb, int K, bool sym,
+                                          const A* tab, int s0, int sb, const int* K, bool sym,
                                           int phi, int u0, int64_t row, const Span& sp,
-                                          A (&mix)[P], A (&sm_m)[P], A (&sm_l)[P],
-                                          A (&sm_num)[P]) {
+                                          A (&mix)[PF], A (&sm_m)[PF], A (&sm_l)[PF],
+                                          A (&sm_num)[PF]) {
   switch (sb) {
-    case 1: do_block_sym<T, A, EPI, 1>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
-    case 2: do_block_sym<T, A, EPI, 2>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
-    case 3: do_block_sym<T, A, EPI, 3>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
-    default: do_block_sym<T, A, EPI, 4>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    case 1: do_block_sym<T, A, EPI, GT, 1>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    case 2: do_block_sym<T, A, EPI, GT, 2>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    case 3: do_block_sym<T, A, EPI, GT, 3>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    case 4: do_block_sym<T, A, EPI, GT, 4>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
+    default: do_block_sym<T, A, EPI, GT, SBMAX>(p, O, xb, tab, s0, K, sym, phi, u0, row, sp, mix, sm_m, sm_l, sm_num); break;
   }
 }
 
@@ -424,26 +468,27 @@ __device__ void lowpass_step(const FwdParams<A>& p, const A* cur, A* nxt, int di
   for (int q = static_cast<int>(threadIdx.x) + org; q < org + span; q += NT) {
     A v = A(0);
     if (q >= -live && q < n + live && q - reach >= org && q + reach < org + span) {
-      v = p.lpp[0] * cur[sidx<PS>(q + ext)];
+      v = p.lpp[0] * cur[(q + ext)];
       if (p.lp_sym) {
         for (int i = 0; i < p.n_lp; ++i) {
           const int t = p.lp_t[i];
-          v = fma(p.lp_p[i], cur[sidx<PS>(q - dil * t + ext)] + cur[sidx<PS>(q + dil * t + ext)],
+          v = fma(p.lp_p[i], cur[(q - dil * t + ext)] + cur[(q + dil * t + ext)],
                   v);
         }
       } else {
         for (int i = 0; i < p.n_lp; ++i) {
           const int t = p.lp_t[i];
-          v = fma(p.lp_p[i], cur[sidx<PS>(q - dil * t + ext)], v);
-          v = fma(p.lp_m[i], cur[sidx<PS>(q + dil * t + ext)], v);
+          v = fma(p.lp_p[i], cur[(q - dil * t + ext)], v);
+          v = fma(p.lp_m[i], cur[(q + dil * t + ext)], v);
         }
       }
     }
-    nxt[sidx<PS>(q + ext)] = v;
+    nxt[(q + ext)] = v;
   }
 }
 
-template <typename T, typename A, int EPI>
+// GT: the octaves' coefficient tables do not fit the shared budget (read from the filters).
+template <typename T, typename A, int EPI, bool GT>
 __global__ void __launch_bounds__(NT, (sizeof(A) == 4 && EPI == EPI_STORE) ? 2 : 1)
 cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -451,8 +496,8 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   A* buf1 = buf0 + p.buf_len;
   A* tab = reinterpret_cast<A*>(smem + p.coef_off);
   A* extra = reinterpret_cast<A*>(smem + p.extra_off);
-  __shared__ int flags[8];
-  __shared__ int kmx[8];  // per scale block: last tap with a nonzero coefficient
+  __shared__ int anti[kMaxScales];   // per scale slot of the octave: antisymmetric halves
+  __shared__ int klast[kMaxScales];  // per scale slot: last tap with a nonzero coefficient
   const int64_t row = blockIdx.x / p.ntile;
   const int tile = static_cast<int>(blockIdx.x - row * p.ntile);
   const int n = static_cast<int>(p.n);
@@ -468,7 +513,7 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   const T* xr = static_cast<const T*>(p.x) + row * p.n;
   for (int i = tid; i < span; i += NT) {
     const int q = sp.org + i;
-    buf0[sidx<PS>(i)] = (q >= 0 && q < n) ? to_acc<T>(xr[q]) : A(0);
+    buf0[(i)] = (q >= 0 && q < n) ? to_acc<T>(xr[q]) : A(0);
   }
   if (EPI == EPI_MIX) {
     for (int i = tid; i < tk; i += NT) extra[i] = A(0);
@@ -486,32 +531,47 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   for (int j = 0; j < p.n_oct; ++j) {
     const Oct& O = p.oct[j];
     if (O.count > 0 && EPI != EPI_PYR) {
-      build_coef<A>(p, O, tab, flags, kmx);
+      build_coef<A>(p, O, tab, anti, klast);
       __syncthreads();
       const int dil = O.dil;
-      const int runs = (static_cast<int>((tk + dil - 1) / dil) + P - 1) / P;
+      const int runs = (static_cast<int>((tk + dil - 1) / dil) + PF - 1) / PF;
       const int items = dil * runs;
       int nblk = 0;
       for (int s0 = 0; s0 < O.count; s0 += block_size(O.count - s0)) ++nblk;
+      const int lg = __ffs(dil) - 1;  // dil = 2^lg
       if (EPI == EPI_STORE) {
-        // spread (block, item) pairs over the threads
-        for (int w = tid; w < nblk * items; w += NT) {
-          const int blk = w / items, it = w % items;
-          int s0 = 0;
-          for (int b = 0; b < blk; ++b) s0 += block_size(O.count - s0);
-          const int phi = it % dil, u0 = (it / dil) * P;
-          if (phi >= tk) continue;
-          A mix[P], m_[P], l_[P], num_[P];
-          run_block<T, A, EPI>(p, O, cur, tab, s0, block_size(O.count - s0), kmx[blk],
-                               flags[blk] == 0, sp.t0 + phi, u0, row, sp, mix, m_, l_, num_);
+        // spread (block, item) pairs over the threads: work unit w = (block, item), walked
+        // incrementally (no divisions)
+        int blk = 0, s0 = 0, it = tid;
+        while (blk < nblk && it >= items) {
+          it -= items;
+          s0 += block_size(O.count - s0);
+          ++blk;
+        }
+        for (; blk < nblk;) {
+          const int sb = block_size(O.count - s0);
+          const int phi = it & (dil - 1), u0 = (it >> lg) * PF;
+          if (phi < tk) {
+            bool sym = true;
+            for (int s = 0; s < sb; ++s) sym = sym && anti[s0 + s] == 0;
+            A mix[PF], m_[PF], l_[PF], num_[PF];
+            run_block<T, A, EPI, GT>(p, O, cur, tab, s0, sb, klast, sym, sp.t0 + phi, u0, row, sp,
+                                     mix, m_, l_, num_);
+          }
+          it += NT;
+          while (blk < nblk && it >= items) {
+            it -= items;
+            s0 += block_size(O.count - s0);
+            ++blk;
+          }
         }
       } else {
         for (int it = tid; it < items; it += NT) {
-          const int phi = it % dil, u0 = (it / dil) * P;
+          const int phi = it & (dil - 1), u0 = (it >> lg) * PF;
           if (phi >= tk) continue;
-          A mix[P], sm_m[P], sm_l[P], sm_num[P];
+          A mix[PF], sm_m[PF], sm_l[PF], sm_num[PF];
 #pragma unroll
-          for (int i = 0; i < P; ++i) {
+          for (int i = 0; i < PF; ++i) {
             const int li = phi + dil * (u0 + i);  // tile-local output index
             mix[i] = A(0);
             if (EPI == EPI_SOFTMAX && li < tk) {
@@ -527,14 +587,14 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
           int s0 = 0;
           for (int b = 0; b < nblk; ++b) {
             const int sb = block_size(O.count - s0);
-            // (the fused epilogues keep the octave's full tap range: the per-block limit made
-            // the mix and softmax kernels slower on B200, 2.04 -> 2.50 ms on cfg4)
-            run_block<T, A, EPI>(p, O, cur, tab, s0, sb, O.half, flags[b] == 0, sp.t0 + phi, u0,
-                                 row, sp, mix, sm_m, sm_l, sm_num);
+            bool sym = true;
+            for (int s = 0; s < sb; ++s) sym = sym && anti[s0 + s] == 0;
+            run_block<T, A, EPI, GT>(p, O, cur, tab, s0, sb, klast, sym, sp.t0 + phi, u0, row, sp,
+                                     mix, sm_m, sm_l, sm_num);
             s0 += sb;
           }
 #pragma unroll
-          for (int i = 0; i < P; ++i) {
+          for (int i = 0; i < PF; ++i) {
             const int li = phi + dil * (u0 + i);
             if (li < tk) {
               if (EPI == EPI_MIX) {
@@ -558,7 +618,7 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
         const int lv = p.oct[j + 1].live;
         A* dst = p.pyr + row * p.pyr_len + p.pyr_off[j + 1] + lv;
         const int lo = max(sp.t0, -lv), hi = min(sp.tend, n + lv);
-        for (int q = lo + tid; q < hi; q += NT) dst[q] = nxt[sidx<PS>(q - sp.org)];
+        for (int q = lo + tid; q < hi; q += NT) dst[q] = nxt[(q - sp.org)];
       }
       A* t = cur;
       cur = nxt;
@@ -692,7 +752,7 @@ size_t fwd_layout(FwdParams<A>& p, const fdwt_morlet_plan* pl, int64_t t_len, in
                   size_t budget) {
   const int64_t span = t_len + 2 * static_cast<int64_t>(halo);
   if (span > 0x3fffffffLL) return 0;
-  p.buf_len = static_cast<int>(padded_len<PS>(span) + 8);
+  p.buf_len = static_cast<int>(span + 8);  // linear buffers (no padding)
   // the coefficient table takes what is left of the shared budget (up to the largest octave)
   int coef = 0;
   if (EPI != EPI_PYR)
@@ -749,7 +809,11 @@ size_t plan_fwd_tiles(FwdParams<A>& p, const fdwt_morlet_plan* pl, int64_t t_bas
 template <typename T, typename A, int EPI>
 int launch_forward(FwdParams<A>& p, int64_t rows, size_t smem, cudaStream_t stream) {
   if (rows * p.ntile > 0x7fffffffLL) return FDWT_ERR_UNSUPPORTED;
-  auto kern = cwt_forward_kernel<T, A, EPI>;
+  bool gt = false;  // some octave's coefficient table does not fit the shared table
+  if (EPI != EPI_PYR)
+    for (int j = 0; j < p.n_oct; ++j)
+      if (p.oct[j].count * (p.oct[j].half + 1) * 4 > p.coef_cap) gt = true;
+  auto kern = gt ? cwt_forward_kernel<T, A, EPI, true> : cwt_forward_kernel<T, A, EPI, false>;
   int st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
   if (st != FDWT_OK) return st;
   if ((st = pre_launch(stream)) != FDWT_OK) return st;
