@@ -559,7 +559,7 @@ class Cfg4(Workload):
         H = m.cwt._filters(x2.device, torch.float32).detach()
         gy = torch.randn_like(x2)
         a, b = m.mag_weight.detach(), m.phase_weight.detach()
-        fma = 3 * _fma_per_position(m.cwt.plan) * x2.numel()
+        fma = 4 * _fma_per_position(m.cwt.plan) * x2.numel()
         return ("cwt_backward_kernel<float,1> + reduce_rows_kernel (mix backward: recompute, "
                 "adjoint, filter gradient)",
                 lambda: _mix_backward(gy, x2, m.cwt.plan, H, a, b, True, True), fma, "fma")
@@ -635,7 +635,7 @@ class Cfg5(Workload):
             V = m.freq_weight.detach()
         out, mm, ll = _softmax_forward(x2, m.cwt.plan, H, V, 19, m.temperature)
         g = torch.randn_like(out)
-        fma = 3 * _fma_per_position(m.cwt.plan) * x2.numel()
+        fma = 4 * _fma_per_position(m.cwt.plan) * x2.numel()
         return ("cwt_backward_kernel<float,2> + reduce_rows_kernel (spectral softmax backward: "
                 "recompute, adjoint, filter gradient)",
                 lambda: _softmax_backward(g, x2, m.cwt.plan, H, V, 19, m.temperature, mm, ll, out,
@@ -841,9 +841,11 @@ def measure_config(W, args, world, dev, barrier, cpu, fp32_peak, batch=None, ful
                            "frac": round(achieved * 1e3 / fp32_peak, 4),
                            "peak_source": "measured in this run: cuBLAS SGEMM 8192^3, TF32 off",
                            "algorithmic_fma_per_call": work,
-                           "fma_count": "3 forward filter-bank passes (recompute W, adjoint, "
-                                        "filter gradient), each sum over scales of (2 * "
-                                        "half-support + 1) FMAs per position after folding",
+                           "fma_count": "4 forward filter-bank passes' worth per position: "
+                                        "recompute W and the adjoint (each sum over scales of "
+                                        "2 * half-support + 1 FMAs after folding the even/odd "
+                                        "taps) and the filter gradient (twice that: separate "
+                                        "re and im gradients for every tap, no folding)",
                            "call_ms": round(k_ms, 4), "launches_per_call": per_call,
                            "traffic": None}
     if not args.no_e2e:
