@@ -30,7 +30,13 @@
 namespace fdwt {
 namespace cwtk {
 
-constexpr int NW = NT / 32;  // warps per CTA
+// Threads of a backward CTA: NT, or NTB_MAX when the row's buffers leave room for one CTA per
+// SM only (more warps to cover the latencies of that CTA).  Device code reads the launched
+// size (nthreads(), nwarps()).
+constexpr int NTB_MAX = 512;
+constexpr int NW_MAX = NTB_MAX / 32;
+__device__ __forceinline__ int nthreads() { return static_cast<int>(blockDim.x); }
+__device__ __forceinline__ int nwarps() { return static_cast<int>(blockDim.x) >> 5; }
 constexpr int KT = 8;        // taps per thread in the filter-gradient reduction
 
 template <typename A>
@@ -154,7 +160,7 @@ __device__ __forceinline__ A block_sum(A v, A* red) {
   __syncthreads();
   A s = A(0);
   if (threadIdx.x == 0)
-    for (int i = 0; i < NW; ++i) s += red[i];
+    for (int i = 0; i < nwarps(); ++i) s += red[i];
   return s;  // valid in thread 0
 }
 
@@ -167,12 +173,12 @@ template <typename A>
 __device__ void build_octave_taps(const FwdParams<A>& f, const Oct& O, A* tab, int* sym,
                                   int* klast) {
   const int K1 = O.half + 1;
-  for (int s = threadIdx.x; s < O.count; s += NT) {
+  for (int s = threadIdx.x; s < O.count; s += nthreads()) {
     sym[s] = 1;
     klast[s] = 0;
   }
   __syncthreads();
-  for (int w = threadIdx.x; w < O.count * K1; w += NT) {
+  for (int w = threadIdx.x; w < O.count * K1; w += nthreads()) {
     const int s = w / K1, k = w - s * K1;
     A t[4];
     fold_coef<A>(f, O, s, k, t);
@@ -195,7 +201,7 @@ __device__ __forceinline__ void stage_gw(const BwdParams<A>& p, int gs, int64_t 
   const int n = static_cast<int>(p.f.n);
   const A* g = p.g + (row * p.f.n_scales + gs) * p.f.n * C;
   constexpr int bytes = static_cast<int>(sizeof(A)) * C;
-  for (int q = threadIdx.x; q < n; q += NT) {
+  for (int q = threadIdx.x; q < n; q += nthreads()) {
     A* d = C == 2 ? gw + 2 * sidx<PS>(q + 1) : gw + sidx<PS>(q + 1);
     const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(d));
     const A* src = g + static_cast<int64_t>(q) * C;
@@ -217,7 +223,7 @@ __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0
 template <typename A>
 __device__ void bwd_lowpass(const FwdParams<A>& f, const A* cur, A* nxt, int dil, int live) {
   const int n = static_cast<int>(f.n);
-  for (int q = static_cast<int>(threadIdx.x) - f.ext; q < n + f.ext; q += NT) {
+  for (int q = static_cast<int>(threadIdx.x) - f.ext; q < n + f.ext; q += nthreads()) {
     A v = A(0);
     if (q >= -live && q < n + live) {
       v = f.lpp[0] * ldE(f, cur, q);
@@ -237,7 +243,7 @@ template <typename A>
 __device__ void bwd_lowpass_adjoint(const FwdParams<A>& f, const A* src, A* dst, int dil,
                                     int live) {
   const int n = static_cast<int>(f.n);
-  for (int q = static_cast<int>(threadIdx.x) - f.ext; q < n + f.ext; q += NT) {
+  for (int q = static_cast<int>(threadIdx.x) - f.ext; q < n + f.ext; q += nthreads()) {
     A v = A(0);
     if (q >= -live && q < n + live) {
       v = f.lpp[0] * ldE(f, src, q);
@@ -253,13 +259,15 @@ __device__ void bwd_lowpass_adjoint(const FwdParams<A>& f, const A* src, A* dst,
 
 // ------------------------------------------------------------------------------ per scale
 
-// (re, im) of one scale at the P outputs n_i = base + dil i, windows read from X (clamped).
-template <typename A, bool SYM>
+// (re, im) of one scale at the P outputs n_i = base + dil i, windows read from X: clamped
+// (CLAMP) or, for items whose windows lie inside the buffer, straight.
+template <typename A, bool SYM, bool CLAMP = true>
 __device__ __forceinline__ void conv_one(const Win& f, const A* X, const A* tab, int K,
                                          int dil, int base, Acc2<A> (&acc)[P]) {
+  auto ld = [&](int pos) { return CLAMP ? ldE(f, X, pos) : X[sidx<PS>(pos + f.ext)]; };
   A L[P], R[P];
 #pragma unroll
-  for (int i = 0; i < P; ++i) L[i] = R[i] = ldE(f, X, base + dil * i);
+  for (int i = 0; i < P; ++i) L[i] = R[i] = ld(base + dil * i);
   {
     alignas(16) A t0[2] = {tab[0], tab[3]};
 #pragma unroll
@@ -275,8 +283,8 @@ __device__ __forceinline__ void conv_one(const Win& f, const A* X, const A* tab,
     for (int i = P - 1; i > 0; --i) L[i] = L[i - 1];
 #pragma unroll
     for (int i = 0; i < P - 1; ++i) R[i] = R[i + 1];
-    L[0] = ldE(f, X, pl);
-    R[P - 1] = ldE(f, X, pr);
+    L[0] = ld(pl);
+    R[P - 1] = ld(pr);
     alignas(16) A t[4] = {tab[4 * k], tab[4 * k + 1], tab[4 * k + 2], tab[4 * k + 3]};
 #pragma unroll
     for (int i = 0; i < P; ++i) {
@@ -341,8 +349,9 @@ __device__ void adjoint_scale(const Win& f, const Oct& O, const A* tab, const A*
   const int runs = static_cast<int>(cdiv(cdiv(len, dil), P));
   const int items = dil * runs;
   using V2 = typename Cplx<A>::type;
-  for (int it = threadIdx.x; it < items; it += NT) {
-    const int phi = it % dil, u0 = (it / dil) * P;
+  const int lg = __ffs(dil) - 1;  // dil = 2^lg
+  for (int it = threadIdx.x; it < items; it += nthreads()) {
+    const int phi = it & (dil - 1), u0 = (it >> lg) * P;
     if (phi >= len) continue;
     const int base = pa + phi + dil * u0;
     V2 L[P], R[P];
@@ -409,11 +418,11 @@ __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, con
   const int runs = dil * ((U + 7) >> 3);
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   using V2 = typename Cplx<A>::type;
-  for (int c = threadIdx.x; c < C * hcols; c += NT) {
+  for (int c = threadIdx.x; c < C * hcols; c += nthreads()) {
     const int k = c % hcols - f.center;
     if (k < -K || k > K) part[c] = A(0);
   }
-  for (int kb = w; kb < nkb; kb += NW) {
+  for (int kb = w; kb < nkb; kb += nwarps()) {
     const int k0 = -K + kb * KT;
     Acc2<A> acc[KT];
 #pragma unroll
@@ -449,12 +458,12 @@ __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, con
 // parameter partials are returned through *pa_sum, *pb_sum (thread-local, summed by caller).
 template <typename A, int EPI, int C, bool SYM>
 __device__ void make_gw(const BwdParams<A>& p, const Oct& O, int s, int gs, const A* X,
-                        const A* tab, A* gw, int64_t row, A& sa, A& sb) {
+                        const A* tab, int ks, A* gw, int64_t row, A& sa, A& sb) {
   const FwdParams<A>& f = p.f;
   const int n = static_cast<int>(f.n);
   if (EPI == EPI_STORE) {
     const A* g = p.g + (row * f.n_scales + gs) * f.n * C;
-    for (int q = threadIdx.x; q < n; q += NT) {
+    for (int q = threadIdx.x; q < n; q += nthreads()) {
       if (C == 2) {
         const typename Cplx<A>::type v = reinterpret_cast<const typename Cplx<A>::type*>(g)[q];
         st_gw<A, C>(gw, q, v.x, v.y);
@@ -478,12 +487,18 @@ __device__ void make_gw(const BwdParams<A>& p, const Oct& O, int s, int gs, cons
     grp = row / f.dim;
     if (!f.v_pos) vconst = static_cast<const A*>(f.a)[(row % f.dim) * f.n_scales + gs];
   }
-  for (int it = threadIdx.x; it < items; it += NT) {
-    const int phi = it % dil, u0 = (it / dil) * P;
+  const int lg = __ffs(dil) - 1;  // dil = 2^lg
+  const Win wf = win(f);
+  for (int it = threadIdx.x; it < items; it += nthreads()) {
+    const int phi = it & (dil - 1), u0 = (it >> lg) * P;
     if (phi >= n) continue;
     const int base = phi + dil * u0;
     Acc2<A> acc[P];
-    conv_one<A, SYM>(win(f), X, tab, O.half, dil, base, acc);
+    // W of the scale up to its last nonzero tap (ks): the taps past it are zero
+    if (base - dil * ks >= -wf.ext && base + dil * (P - 1 + ks) <= n + wf.ext - 1)
+      conv_one<A, SYM, false>(wf, X, tab, ks, dil, base, acc);
+    else
+      conv_one<A, SYM, true>(wf, X, tab, ks, dil, base, acc);
 #pragma unroll
     for (int i = 0; i < P; ++i) {
       const int q = base + dil * i;
@@ -546,7 +561,7 @@ __device__ void scale_pass(const BwdParams<A>& p, const Oct& O, int live, int s,
   const FwdParams<A>& f = p.f;
   const int gs = f.order[O.begin + s];
   A sa = A(0), sb = A(0);
-  make_gw<A, EPI, C, SYM>(p, O, s, gs, X, tab, gw, row, sa, sb);
+  make_gw<A, EPI, C, SYM>(p, O, s, gs, X, tab, ks, gw, row, sa, sb);
   if (EPI == EPI_MIX) {
     const A ta = block_sum(sa, red);
     const A tb = block_sum(sb, red);
@@ -595,7 +610,7 @@ __device__ void octave_pass(const BwdParams<A>& p, const Oct& O, int live, A* G,
 }
 
 template <typename A, int EPI>
-__global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant__ BwdParams<A> p) {
+__global__ void __launch_bounds__(NTB_MAX) cwt_backward_kernel(const __grid_constant__ BwdParams<A> p) {
   extern __shared__ __align__(16) unsigned char smem[];
   const FwdParams<A>& f = p.f;
   A* bufs[3] = {reinterpret_cast<A*>(smem), reinterpret_cast<A*>(smem) + f.buf_len,
@@ -613,14 +628,14 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
   const A* xr = static_cast<const A*>(f.x) + row * f.n;
 
   // the end cells of the dL/dW buffers (positions -1 and n) are never written again
-  for (int q = threadIdx.x; q < (EPI == EPI_STORE ? 2 : 1) * p.gw_len; q += NT) gws[0][q] = A(0);
+  for (int q = threadIdx.x; q < (EPI == EPI_STORE ? 2 : 1) * p.gw_len; q += nthreads()) gws[0][q] = A(0);
   __syncthreads();
 
   // pass 1: x_1 .. x_{J-1} into the row's scratch
   if (p.need_x && J > 1) {
     A* cur = bufs[0];
     A* nxt = bufs[1];
-    for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += NT)
+    for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += nthreads())
       atE(f, cur, q) = (q >= 0 && q < n) ? xr[q] : A(0);
     __syncthreads();
     for (int j = 0; j + 1 < J; ++j) {
@@ -629,7 +644,7 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
       if (p.pyr_off[j + 1] >= 0) {
         const int lv = f.oct[j + 1].live;
         A* dst = p.pyr + row * p.pyr_len + p.pyr_off[j + 1];
-        for (int q = static_cast<int>(threadIdx.x) - lv; q < n + lv; q += NT)
+        for (int q = static_cast<int>(threadIdx.x) - lv; q < n + lv; q += nthreads())
           dst[q + lv] = atE(f, nxt, q);
       }
       A* t = cur;
@@ -643,7 +658,7 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
   A* G = bufs[0];
   A* Gn = bufs[1];
   A* X = bufs[2];
-  for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += NT) atE(f, G, q) = A(0);
+  for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += nthreads()) atE(f, G, q) = A(0);
   for (int j = J - 1; j >= 0; --j) {
     const Oct& O = f.oct[j];
     if (j + 1 < J && p.need_gx) {
@@ -663,7 +678,7 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
       if (p.need_x) {
         const int lv = O.live;
         const A* srcp = j == 0 ? xr : p.pyr + row * p.pyr_len + p.pyr_off[j];
-        for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += NT)
+        for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += nthreads())
           atE(f, X, q) = (q >= -lv && q < n + lv) ? srcp[q + lv] : A(0);
       }
       __syncthreads();
@@ -677,7 +692,7 @@ __global__ void __launch_bounds__(NT) cwt_backward_kernel(const __grid_constant_
   __syncthreads();
   if (p.need_gx) {
     A* gx = p.gx + row * f.n;
-    for (int q = threadIdx.x; q < n; q += NT) gx[q] = atE(f, G, q);
+    for (int q = threadIdx.x; q < n; q += nthreads()) gx[q] = atE(f, G, q);
   }
 }
 
@@ -797,7 +812,7 @@ size_t row_bwd_smem(int64_t n, const fdwt_morlet_plan* pl, int ext, BwdParams<A>
   off += tab * sizeof(A);
   off = (off + 15) / 16 * 16;
   const size_t red_off = off;
-  off += NW * sizeof(A);
+  off += NW_MAX * sizeof(A);
   if (p) {
     p->f.buf_len = static_cast<int>(buf_len);
     p->gw_len = static_cast<int>(gw_len);
@@ -919,7 +934,9 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   st = allow_max_dynamic_smem(reinterpret_cast<const void*>(kern));
   if (st != FDWT_OK) return st;
   if ((st = pre_launch(stream)) != FDWT_OK) return st;
-  kern<<<static_cast<unsigned>(rows), NT, smem, stream>>>(p);
+  // one CTA per SM when the row needs more than half the shared memory: give it NTB_MAX threads
+  const int threads = smem > budget / 2 ? NTB_MAX : NT;
+  kern<<<static_cast<unsigned>(rows), threads, smem, stream>>>(p);
   if ((st = launch_status()) != FDWT_OK) return st;
   if (gh && (st = reduce_rows<A>(ghp, rows, ghcols, 1, static_cast<A*>(gh), tmp, stream)) != FDWT_OK)
     return st;

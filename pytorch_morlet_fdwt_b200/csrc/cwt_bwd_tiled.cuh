@@ -58,11 +58,11 @@ __device__ void gradh_tile(const Oct& O, int center, const A* X, int xorg, int x
   const int runs = dil * ((U + 7) >> 3);
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   using V2 = typename Cplx<A>::type;
-  for (int c = threadIdx.x; c < C * hcols; c += NT) {
+  for (int c = threadIdx.x; c < C * hcols; c += nthreads()) {
     const int k = c % hcols - center;
     if (k < -K || k > K) part[c] = A(0);
   }
-  for (int kb = w; kb < nkb; kb += NW) {
+  for (int kb = w; kb < nkb; kb += nwarps()) {
     const int k0 = -K + kb * KT;
     Acc2<A> acc[KT];
 #pragma unroll
@@ -121,7 +121,7 @@ __device__ void make_gw_tile(const BwdParams<A>& p, const Oct& O, int gs, const 
   const int n = static_cast<int>(f.n);
   if (EPI == EPI_STORE) {
     const A* g = p.g + (row * f.n_scales + gs) * f.n * C;
-    for (int v = threadIdx.x; v < nv; v += NT) {
+    for (int v = threadIdx.x; v < nv; v += nthreads()) {
       const int a = o + v;
       A re = A(0), im = A(0);
       if (a >= 0 && a < n) {
@@ -146,8 +146,9 @@ __device__ void make_gw_tile(const BwdParams<A>& p, const Oct& O, int gs, const 
     grp = row / f.dim;
     if (!f.v_pos) vconst = static_cast<const A*>(f.a)[(row % f.dim) * f.n_scales + gs];
   }
-  for (int it = threadIdx.x; it < items; it += NT) {
-    const int phi = it % dil, u0 = (it / dil) * P;
+  const int lg = __ffs(dil) - 1;  // dil = 2^lg
+  for (int it = threadIdx.x; it < items; it += nthreads()) {
+    const int phi = it & (dil - 1), u0 = (it >> lg) * P;
     if (phi >= nv) continue;
     const int base = phi + dil * u0;
     Acc2<A> acc[P];
@@ -278,22 +279,22 @@ __global__ void __launch_bounds__(NT) cwt_octave_bwd_kernel(const __grid_constan
   if (p.need_x && O.count > 0) {  // X = x_j, zero outside [-live_j, n + live_j)
     const A* src = q.j == 0 ? static_cast<const A*>(f.x) + row * f.n
                             : p.pyr + row * p.pyr_len + p.pyr_off[q.j] + live;
-    for (int i = tid; i < tk + 2 * q.XH; i += NT) {
+    for (int i = tid; i < tk + 2 * q.XH; i += nthreads()) {
       const int a = t0 - q.XH + i;
       X[sidx<PS>(i)] = (a >= -live && a < n + live) ? src[a] : A(0);
     }
   }
   if (has_in) {
     const A* gi = q.g_in + row * q.g_stride + q.e;
-    for (int i = tid; i < tk + 2 * q.R; i += NT) {
+    for (int i = tid; i < tk + 2 * q.R; i += nthreads()) {
       const int a = t0 - q.R + i;
       Gp[sidx<PS>(i)] = (a >= -q.e && a < n + q.e) ? gi[a] : A(0);
     }
   }
-  for (int i = tid; i < q.gw_len; i += NT) gw[i] = A(0);  // the window's end cells stay zero
+  for (int i = tid; i < q.gw_len; i += nthreads()) gw[i] = A(0);  // the window's end cells stay zero
   __syncthreads();
   if (p.need_gx) {  // Go = LP_j^T G_{j+1} on the owned positions inside live_j
-    for (int i = tid; i < tk; i += NT) {
+    for (int i = tid; i < tk; i += nthreads()) {
       const int a = t0 + i;
       A v = A(0);
       if (has_in && a >= -live && a < n + live) {
@@ -320,13 +321,13 @@ __global__ void __launch_bounds__(NT) cwt_octave_bwd_kernel(const __grid_constan
   if (p.need_gx) {
     if (q.g_out) {
       A* go = q.g_out + row * q.g_stride + q.e;
-      for (int i = tid; i < tk; i += NT) {
+      for (int i = tid; i < tk; i += nthreads()) {
         const int a = t0 + i;
         if (a < n + q.e) go[a] = Go[sidx<PS>(i)];
       }
     } else {
       A* gx = p.gx + row * f.n;
-      for (int i = tid; i < tk; i += NT) {
+      for (int i = tid; i < tk; i += nthreads()) {
         const int a = t0 + i;
         if (a >= 0 && a < n) gx[a] = Go[sidx<PS>(i)];
       }
@@ -362,7 +363,7 @@ size_t oct_layout(OctParams<A>& q, const fdwt_morlet_plan* pl, int j, int t_len,
   q.gp_off = region(q.R > 0 ? static_cast<size_t>(padded_len<PS>(t_len + 2 * q.R)) + 8 : 0);
   q.go_off = region(need_gx ? static_cast<size_t>(padded_len<PS>(t_len)) + 8 : 0);
   q.tab_off = region(4 * static_cast<size_t>(cnt) * (pl->oct_half[j] + 1));
-  q.red_off = region(NW);
+  q.red_off = region(NW_MAX);
   const size_t smem = off + 16;
   return smem > budget ? 0 : smem;
 }
