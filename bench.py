@@ -552,17 +552,17 @@ class Cfg4(Workload):
 
     def kernel(self, st):
         import torch
-        from pytorch_morlet_fdwt_b200.cwt import _mix_backward
+        from pytorch_morlet_fdwt_b200.cwt import _mix_tokens_backward
         m = st["m"]
-        B = st["x"].shape[0]
-        x2 = st["x"].detach().transpose(1, 2).reshape(-1, self.shape[0]).contiguous()
-        H = m.cwt._filters(x2.device, torch.float32).detach()
-        gy = torch.randn_like(x2)
+        x = st["x"].detach()  # (B, L, D) tokens, read in place by the kernels
+        H = m.cwt._filters(x.device, torch.float32).detach()
+        gy = torch.randn_like(x)
         a, b = m.mag_weight.detach(), m.phase_weight.detach()
-        fma = 4 * _fma_per_position(m.cwt.plan) * x2.numel()
-        return ("cwt_backward_kernel<float,1> + reduce_rows_kernel (mix backward: recompute, "
-                "adjoint, filter gradient)",
-                lambda: _mix_backward(gy, x2, m.cwt.plan, H, a, b, True, True), fma, "fma")
+        fma = 4 * _fma_per_position(m.cwt.plan) * x.numel()
+        return ("cwt_backward_kernel<float,1> + tokens_to_rows_kernel + reduce_rows_kernel (mix "
+                "backward on the token layout: recompute, adjoint, filter gradient)",
+                lambda: _mix_tokens_backward(gy, x, m.cwt.plan, H, a, b, True, True, True), fma,
+                "fma")
 
     def cpu(self, ref, sample):
         import torch

@@ -246,6 +246,23 @@ int fdwt_mix_backward(int dtype, int64_t rows, int64_t n, const void* x, const v
                       const void* gy, void* gx, void* gh, void* ga, void* gb, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* MorletTokenMixer's layout.  x and y are (batch, n, dim) tensors, channel d of token q of item
+ * b at (b*n + q)*dim + d, and y gets bias[d] added (bias may be null).  The reference
+ * transposes x to (batch, dim, n) rows, calls morlet_mix, transposes back and adds the bias in
+ * separate torch kernels (fdwt/layers.py:49-55); here the kernels read and write the token
+ * layout themselves.  The backward takes dL/dy (batch, n, dim) and returns dL/dx in the same
+ * layout, dL/dH, dL/da, dL/db (dim, n_scales) and dL/dbias (dim; null skips it). */
+int fdwt_mix_tokens_forward(int dtype, int64_t batch, int64_t n, int64_t dim, const void* x,
+                            const void* filters, const fdwt_morlet_plan* plan, const void* a,
+                            const void* b, const void* bias, void* y, void* stream);
+size_t fdwt_mix_tokens_backward_workspace(int dtype, int64_t batch, int64_t n, int64_t dim,
+                                          const fdwt_morlet_plan* plan, int need_gh);
+int fdwt_mix_tokens_backward(int dtype, int64_t batch, int64_t n, int64_t dim, const void* x,
+                             const void* filters, const fdwt_morlet_plan* plan, const void* a,
+                             const void* b, const void* gy, void* gx, void* gh, void* ga,
+                             void* gb, void* gbias, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* Backward of fdwt_specsoftmax_forward from dL/dout (rows, n), given the forward's out, m and
  * l: dL/dx, dL/dH and dL/dV (the shape of V).  Replaces backward_stage
  * (fdwt/kernels/softmax.py:206-210) and the octave loop of _SpectralSoftmaxFunction.backward

@@ -12,14 +12,14 @@ template <int EPI>
 int dispatch_forward(int dtype, int64_t rows, int64_t n, const void* x, const void* h,
                      const fdwt_morlet_plan* pl, void* y, const void* a, const void* b,
                      void* m, void* l, int64_t dim, int v_pos, double inv_tau,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int tok = 0, const void* bias = nullptr) {
   switch (dtype) {
     case FDWT_F32:
       return run_forward<float, float, EPI>(rows, n, x, h, pl, y, a, b, m, l, dim, v_pos, inv_tau,
-                                            stream);
+                                            stream, tok, bias);
     case FDWT_F64:
       return run_forward<double, double, EPI>(rows, n, x, h, pl, y, a, b, m, l, dim, v_pos,
-                                              inv_tau, stream);
+                                              inv_tau, stream, tok, bias);
     default:
       return FDWT_ERR_UNSUPPORTED;
   }
@@ -166,4 +166,67 @@ extern "C" int fdwt_specsoftmax_backward(int dtype, int64_t rows, int64_t n, con
                                         nullptr, nullptr, gv, gh != nullptr, workspace,
                                         workspace_bytes, static_cast<cudaStream_t>(stream),
                                         nullptr);
+}
+
+// MorletTokenMixer's layout: x, y, dL/dy and dL/dx are (batch, n, dim) tensors (the reference
+// transposes them to (batch, dim, n) rows around morlet_mix, fdwt/layers.py:49-55).
+extern "C" int fdwt_mix_tokens_forward(int dtype, int64_t batch, int64_t n, int64_t dim,
+                                       const void* x, const void* filters,
+                                       const fdwt_morlet_plan* plan, const void* a,
+                                       const void* b, const void* bias, void* y, void* stream) {
+  if (batch < 0 || dim < 1 || batch > 0x7fffffffLL / dim) return FDWT_ERR_INVALID;
+  if (batch > 0 && (x == nullptr || filters == nullptr || y == nullptr || a == nullptr ||
+                    b == nullptr))
+    return FDWT_ERR_INVALID;
+  return dispatch_forward<EPI_MIX>(dtype, batch * dim, n, x, filters, plan, y, a, b, nullptr,
+                                   nullptr, dim, 0, 1.0, static_cast<cudaStream_t>(stream), 1,
+                                   bias);
+}
+
+namespace {
+int dispatch_tokens_backward(int dtype, int64_t batch, int64_t n, int64_t dim, const void* x,
+                             const void* h, const fdwt_morlet_plan* pl, const void* a,
+                             const void* b, const void* gy, void* gx, void* gh, void* ga,
+                             void* gb, void* gbias, bool need_h, void* ws, size_t ws_bytes,
+                             cudaStream_t stream, size_t* need) {
+  switch (dtype) {
+    case FDWT_F32:
+      return run_mix_tokens_backward<float>(batch, n, dim, x, h, pl, a, b, gy, gx, gh, ga, gb,
+                                            gbias, need_h, ws, ws_bytes, stream, need);
+    case FDWT_F64:
+      return run_mix_tokens_backward<double>(batch, n, dim, x, h, pl, a, b, gy, gx, gh, ga, gb,
+                                             gbias, need_h, ws, ws_bytes, stream, need);
+    default:
+      return FDWT_ERR_UNSUPPORTED;
+  }
+}
+}  // namespace
+
+extern "C" size_t fdwt_mix_tokens_backward_workspace(int dtype, int64_t batch, int64_t n,
+                                                     int64_t dim, const fdwt_morlet_plan* plan,
+                                                     int need_gh) {
+  size_t need = 0;
+  if (check_plan(plan, n) != FDWT_OK) return 0;
+  if (dispatch_tokens_backward(dtype, batch, n, dim, nullptr, nullptr, plan, nullptr, nullptr,
+                               nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                               need_gh != 0, nullptr, 0, nullptr, &need) != FDWT_OK)
+    return 0;
+  return need;
+}
+
+extern "C" int fdwt_mix_tokens_backward(int dtype, int64_t batch, int64_t n, int64_t dim,
+                                        const void* x, const void* filters,
+                                        const fdwt_morlet_plan* plan, const void* a,
+                                        const void* b, const void* gy, void* gx, void* gh,
+                                        void* ga, void* gb, void* gbias, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (batch < 0 || dim < 1) return FDWT_ERR_INVALID;
+  if (batch > 0 && (x == nullptr || filters == nullptr || a == nullptr || b == nullptr ||
+                    gy == nullptr))
+    return FDWT_ERR_INVALID;
+  const int st = check_plan(plan, n);
+  if (st != FDWT_OK) return st;
+  return dispatch_tokens_backward(dtype, batch, n, dim, x, filters, plan, a, b, gy, gx, gh, ga,
+                                  gb, gbias, gh != nullptr, workspace, workspace_bytes,
+                                  static_cast<cudaStream_t>(stream), nullptr);
 }

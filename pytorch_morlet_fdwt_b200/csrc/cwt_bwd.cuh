@@ -625,7 +625,7 @@ __global__ void __launch_bounds__(NTB_MAX) cwt_backward_kernel(const __grid_cons
   const int n = static_cast<int>(f.n);
   const int E = f.ext;
   const int J = f.n_oct;
-  const A* xr = static_cast<const A*>(f.x) + row * f.n;
+  const RowRef<const A> xr = row_ref(static_cast<const A*>(f.x), f, row);
 
   // the end cells of the dL/dW buffers (positions -1 and n) are never written again
   for (int q = threadIdx.x; q < (EPI == EPI_STORE ? 2 : 1) * p.gw_len; q += nthreads()) gws[0][q] = A(0);
@@ -675,9 +675,12 @@ __global__ void __launch_bounds__(NTB_MAX) cwt_backward_kernel(const __grid_cons
       cp_commit();
     }
     if (O.count > 0) {
-      if (p.need_x) {
+      if (p.need_x && j == 0) {  // x_0 = x on [0, n)
+        for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += nthreads())
+          atE(f, X, q) = (q >= 0 && q < n) ? xr[q] : A(0);
+      } else if (p.need_x) {
         const int lv = O.live;
-        const A* srcp = j == 0 ? xr : p.pyr + row * p.pyr_len + p.pyr_off[j];
+        const A* srcp = p.pyr + row * p.pyr_len + p.pyr_off[j];
         for (int q = static_cast<int>(threadIdx.x) - E; q < n + E; q += nthreads())
           atE(f, X, q) = (q >= -lv && q < n + lv) ? srcp[q + lv] : A(0);
       }
@@ -691,7 +694,7 @@ __global__ void __launch_bounds__(NTB_MAX) cwt_backward_kernel(const __grid_cons
   }
   __syncthreads();
   if (p.need_gx) {
-    A* gx = p.gx + row * f.n;
+    const RowRef<A> gx = row_ref(p.gx, f, row);
     for (int q = threadIdx.x; q < n; q += nthreads()) gx[q] = atE(f, G, q);
   }
 }
@@ -829,7 +832,7 @@ int run_backward_tiled(int64_t rows, int64_t n, const void* x, const void* h,
                        const void* b, int64_t dim, int v_pos, double inv_tau, const void* g,
                        const void* sm_m, const void* sm_l, const void* sm_out, void* gx, void* gh,
                        void* ga, void* gb, void* gv, bool need_h, void* ws, size_t ws_bytes,
-                       cudaStream_t stream, size_t* ws_needed);
+                       cudaStream_t stream, size_t* ws_needed, int tok);
 
 // Backward of the transform (EPI_STORE), of the mix (EPI_MIX) or of the spectral softmax
 // (EPI_SOFTMAX).  Rows whose buffers do not fit one CTA's shared memory take the octave-tiled
@@ -841,7 +844,8 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
                  const fdwt_morlet_plan* pl, const void* a, const void* b, int64_t dim,
                  int v_pos, double inv_tau, const void* g, const void* sm_m, const void* sm_l,
                  const void* sm_out, void* gx, void* gh, void* ga, void* gb, void* gv, bool need_h,
-                 void* ws, size_t ws_bytes, cudaStream_t stream, size_t* ws_needed) {
+                 void* ws, size_t ws_bytes, cudaStream_t stream, size_t* ws_needed,
+                 int tok = 0) {
   int st = check_plan(pl, n);
   if (st != FDWT_OK) return st;
   if (EPI == EPI_SOFTMAX && pl->channels != 2) return FDWT_ERR_INVALID;
@@ -858,7 +862,7 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
     if (tiled)
       return run_backward_tiled<A, EPI>(rows, n, x, h, pl, geo, a, b, dim, v_pos, inv_tau, g,
                                         sm_m, sm_l, sm_out, gx, gh, ga, gb, gv, need_h, ws,
-                                        ws_bytes, stream, ws_needed);
+                                        ws_bytes, stream, ws_needed, tok);
     *ws_needed = lay.total;
     return FDWT_OK;
   }
@@ -892,7 +896,7 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   if (tiled)
     return run_backward_tiled<A, EPI>(rows, n, x, h, pl, geo, a, b, dim, v_pos, inv_tau, g, sm_m,
                                       sm_l, sm_out, gx, gh, ga, gb, gv, need_h, ws, ws_bytes,
-                                      stream, nullptr);
+                                      stream, nullptr, tok);
   if (lay.total > 0 && (ws == nullptr || ws_bytes < lay.total)) return FDWT_ERR_WORKSPACE;
   unsigned char* w = static_cast<unsigned char*>(ws);
   A* pyr = reinterpret_cast<A*>(w);
@@ -913,6 +917,7 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   p.f.dim = dim;
   p.f.v_pos = v_pos;
   p.f.inv_tau = static_cast<A>(inv_tau);
+  p.f.tok = tok;
   p.g = static_cast<const A*>(g);
   p.sm_m = static_cast<const A*>(sm_m);
   p.sm_l = static_cast<const A*>(sm_l);
@@ -950,6 +955,108 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
       (st = reduce_rows<A>(pv, rows, S, dim, static_cast<A*>(gv), tmp, stream)) != FDWT_OK)
     return st;
   return FDWT_OK;
+}
+
+// ------------------------------------------------------------------------------ token layout
+
+// dL/dy of MorletTokenMixer's (B, n, dim) output into the (B dim, n) rows the backward reads
+// once per scale, and the column sums of each (b, 32-position) tile for dL/dbias: 32 x 32
+// tiles through shared memory (coalesced on both sides), 32 x 8 threads.
+template <typename A>
+__global__ void __launch_bounds__(256) tokens_to_rows_kernel(const A* __restrict__ in, int64_t B,
+                                                             int64_t n, int64_t dim,
+                                                             A* __restrict__ out,
+                                                             A* __restrict__ colsum) {
+  __shared__ A t[32][33];
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 32;
+  const int64_t d0 = static_cast<int64_t>(blockIdx.y) * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int64_t b = blockIdx.z; b < B; b += gridDim.z) {
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t q = q0 + i, d = d0 + tx;
+      t[i][tx] = (q < n && d < dim) ? in[(b * n + q) * dim + d] : A(0);
+    }
+    __syncthreads();
+    if (ty == 0 && d0 + tx < dim) {
+      A v = A(0);
+      for (int i = 0; i < 32; ++i) v += t[i][tx];
+      colsum[(b * gridDim.x + blockIdx.x) * dim + d0 + tx] = v;
+    }
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t d = d0 + i, q = q0 + tx;
+      if (d < dim && q < n) out[(b * dim + d) * n + q] = t[tx][i];
+    }
+    __syncthreads();
+  }
+}
+
+// Workspace of the token-layout mix backward: dL/dy rows, tile column sums, their reduction
+// scratch, then the mix backward's own regions.
+struct TokLayout {
+  size_t rows_bytes = 0, colsum = 0, tmp = 0, head = 0;
+};
+template <typename A>
+TokLayout tok_layout(int64_t B, int64_t n, int64_t dim) {
+  TokLayout L;
+  const int64_t ntq = cdiv(n, 32);
+  L.rows_bytes = align256(static_cast<size_t>(B * dim) * n * sizeof(A));
+  L.colsum = align256(static_cast<size_t>(B * ntq) * dim * sizeof(A));
+  L.tmp = align256(reduce_tmp_elems(B * ntq, dim, 1) * sizeof(A));
+  L.head = L.rows_bytes + L.colsum + L.tmp;
+  return L;
+}
+
+// Backward of the mix on MorletTokenMixer's layout: x, dL/dy, dL/dx are (B, n, dim); dL/dbias
+// (dim) is the sum of dL/dy over (B, n).  ws_needed != null: only report the workspace size.
+template <typename A>
+int run_mix_tokens_backward(int64_t B, int64_t n, int64_t dim, const void* x, const void* h,
+                            const fdwt_morlet_plan* pl, const void* a, const void* b,
+                            const void* gy, void* gx, void* gh, void* ga, void* gb, void* gbias,
+                            bool need_h, void* ws, size_t ws_bytes, cudaStream_t stream,
+                            size_t* ws_needed) {
+  if (B < 0 || n < 1 || dim < 1 || B > 0x7fffffffLL / dim) return FDWT_ERR_INVALID;
+  const int64_t rows = B * dim;
+  const TokLayout T = tok_layout<A>(B, n, dim);
+  size_t inner = 0;
+  int st = run_backward<A, EPI_MIX>(rows, n, nullptr, nullptr, pl, nullptr, nullptr, dim, 0, 1.0,
+                                    nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                    nullptr, nullptr, need_h, nullptr, 0, nullptr, &inner, 1);
+  if (st != FDWT_OK) return st;
+  if (ws_needed) {
+    *ws_needed = T.head + inner;
+    return FDWT_OK;
+  }
+  if (B == 0) {
+    if (gbias) {
+      const cudaError_t e = cudaMemsetAsync(gbias, 0, dim * sizeof(A), stream);
+      if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return FDWT_ERR_CUDA;
+      }
+    }
+    return run_backward<A, EPI_MIX>(0, n, x, h, pl, a, b, dim, 0, 1.0, gy, nullptr, nullptr,
+                                    nullptr, gx, gh, ga, gb, nullptr, need_h, nullptr, 0, stream,
+                                    nullptr, 1);
+  }
+  if (ws == nullptr || ws_bytes < T.head + inner) return FDWT_ERR_WORKSPACE;
+  unsigned char* w = static_cast<unsigned char*>(ws);
+  A* gy_rows = reinterpret_cast<A*>(w);
+  A* colsum = reinterpret_cast<A*>(w + T.rows_bytes);
+  A* tmp = reinterpret_cast<A*>(w + T.rows_bytes + T.colsum);
+  const int64_t ntq = cdiv(n, 32), ntd = cdiv(dim, 32);
+  if (ntq > 0x7fffffffLL || ntd > 65535) return FDWT_ERR_UNSUPPORTED;
+  if ((st = pre_launch(stream)) != FDWT_OK) return st;
+  tokens_to_rows_kernel<A><<<dim3(static_cast<unsigned>(ntq), static_cast<unsigned>(ntd),
+                                  static_cast<unsigned>(imin(B, 65535))),
+                             dim3(32, 8), 0, stream>>>(static_cast<const A*>(gy), B, n, dim,
+                                                       gy_rows, colsum);
+  if ((st = launch_status()) != FDWT_OK) return st;
+  if (gbias && (st = reduce_rows<A>(colsum, B * ntq, dim, 1, static_cast<A*>(gbias), tmp,
+                                    stream)) != FDWT_OK)
+    return st;
+  return run_backward<A, EPI_MIX>(rows, n, x, h, pl, a, b, dim, 0, 1.0, gy_rows, nullptr, nullptr,
+                                  nullptr, gx, gh, ga, gb, nullptr, need_h, w + T.head, inner,
+                                  stream, nullptr, 1);
 }
 
 }  // namespace cwtk

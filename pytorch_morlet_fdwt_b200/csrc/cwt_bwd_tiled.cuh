@@ -277,8 +277,9 @@ __global__ void __launch_bounds__(NT) cwt_octave_bwd_kernel(const __grid_constan
   const bool has_in = p.need_gx && q.g_in != nullptr;
 
   if (p.need_x && O.count > 0) {  // X = x_j, zero outside [-live_j, n + live_j)
-    const A* src = q.j == 0 ? static_cast<const A*>(f.x) + row * f.n
-                            : p.pyr + row * p.pyr_len + p.pyr_off[q.j] + live;
+    const RowRef<const A> src =
+        q.j == 0 ? row_ref(static_cast<const A*>(f.x), f, row)
+                 : RowRef<const A>{p.pyr + row * p.pyr_len + p.pyr_off[q.j] + live, 1};
     for (int i = tid; i < tk + 2 * q.XH; i += nthreads()) {
       const int a = t0 - q.XH + i;
       X[sidx<PS>(i)] = (a >= -live && a < n + live) ? src[a] : A(0);
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(NT) cwt_octave_bwd_kernel(const __grid_constan
         if (a < n + q.e) go[a] = Go[sidx<PS>(i)];
       }
     } else {
-      A* gx = p.gx + row * f.n;
+      const RowRef<A> gx = row_ref(p.gx, f, row);
       for (int i = tid; i < tk; i += nthreads()) {
         const int a = t0 + i;
         if (a >= 0 && a < n) gx[a] = Go[sidx<PS>(i)];
@@ -376,7 +377,7 @@ int run_backward_tiled(int64_t rows, int64_t n, const void* x, const void* h,
                        const void* b, int64_t dim, int v_pos, double inv_tau, const void* g,
                        const void* sm_m, const void* sm_l, const void* sm_out, void* gx, void* gh,
                        void* ga, void* gb, void* gv, bool need_h, void* ws, size_t ws_bytes,
-                       cudaStream_t stream, size_t* ws_needed) {
+                       cudaStream_t stream, size_t* ws_needed, int tok) {
   const int J = pl->n_octaves;
   const bool need_gx = ws_needed ? true : gx != nullptr;
   const bool need_x = need_h || EPI != EPI_STORE;
@@ -443,7 +444,8 @@ int run_backward_tiled(int64_t rows, int64_t n, const void* x, const void* h,
 
   int st;
   if (need_x && J > 1 && lay.pyr_len > 0 &&
-      (st = run_pyramid<A>(rows, n, x, pl, geo, pyr, lay.pyr_len, lay.pyr_off, stream)) != FDWT_OK)
+      (st = run_pyramid<A>(rows, n, x, pl, geo, pyr, lay.pyr_len, lay.pyr_off, stream, tok,
+                           dim)) != FDWT_OK)
     return st;
 
   BwdParams<A>& p = q.b;
@@ -456,6 +458,7 @@ int run_backward_tiled(int64_t rows, int64_t n, const void* x, const void* h,
   p.f.dim = dim;
   p.f.v_pos = v_pos;
   p.f.inv_tau = static_cast<A>(inv_tau);
+  p.f.tok = tok;
   p.g = static_cast<const A*>(g);
   p.sm_m = static_cast<const A*>(sm_m);
   p.sm_l = static_cast<const A*>(sm_l);

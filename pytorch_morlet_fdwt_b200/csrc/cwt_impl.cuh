@@ -106,7 +106,24 @@ struct FwdParams {
   A* pyr;
   int64_t pyr_len;
   int32_t pyr_off[kMaxOct];
+  // token layout (MorletTokenMixer's (B, n, dim) input): x, and MIX's y, hold row b dim + d at
+  // element stride dim (element q at (b n + q) dim + d); MIX adds bias[d] to y when non-null
+  int32_t tok;
+  const void* bias;
 };
+
+// Row `row` of a signal argument: (rows, n) row-major, or the token layout of FwdParams::tok.
+template <typename T>
+struct RowRef {
+  T* p;
+  int64_t step;
+  __device__ __forceinline__ T& operator[](int64_t q) const { return p[q * step]; }
+};
+template <typename T, typename P>
+__device__ __forceinline__ RowRef<T> row_ref(T* base, const P& f, int64_t row) {
+  if (f.tok) return RowRef<T>{base + (row / f.dim) * f.n * f.dim + row % f.dim, f.dim};
+  return RowRef<T>{base + row * f.n, 1};
+}
 
 // The part of a row a CTA computes: buffers cover [org, org + span); kept outputs [t0, tend).
 struct Span {
@@ -510,7 +527,7 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   const int span = tk + 2 * p.halo;
   sp.limit = sp.org + span - 1;
 
-  const T* xr = static_cast<const T*>(p.x) + row * p.n;
+  const RowRef<const T> xr = row_ref(static_cast<const T*>(p.x), p, row);
   for (int i = tid; i < span; i += NT) {
     const int q = sp.org + i;
     buf0[(i)] = (q >= 0 && q < n) ? to_acc<T>(xr[q]) : A(0);
@@ -627,8 +644,9 @@ cwt_forward_kernel(const __grid_constant__ FwdParams<A> p) {
   }
 
   if (EPI == EPI_MIX) {
-    A* yr = static_cast<A*>(p.y) + row * p.n + sp.t0;
-    for (int i = tid; i < tk; i += NT) yr[i] = extra[i];
+    const RowRef<A> yr = row_ref(static_cast<A*>(p.y), p, row);
+    const A bias = p.bias ? static_cast<const A*>(p.bias)[row % p.dim] : A(0);
+    for (int i = tid; i < tk; i += NT) yr[sp.t0 + i] = extra[i] + bias;
   } else if (EPI == EPI_SOFTMAX) {
     A* o = static_cast<A*>(p.y) + row * p.n + sp.t0;
     A* mo = static_cast<A*>(p.m_out) + row * p.n + sp.t0;
@@ -825,7 +843,7 @@ template <typename T, typename A, int EPI>
 int run_forward(int64_t rows, int64_t n, const void* x, const void* h,
                 const fdwt_morlet_plan* pl, void* y, const void* a, const void* b,
                 void* m_out, void* l_out, int64_t dim, int v_pos, double inv_tau,
-                cudaStream_t stream) {
+                cudaStream_t stream, int tok = 0, const void* bias = nullptr) {
   int st = check_plan(pl, n);
   if (st != FDWT_OK) return st;
   if (rows == 0) return FDWT_OK;
@@ -844,6 +862,8 @@ int run_forward(int64_t rows, int64_t n, const void* x, const void* h,
   p.dim = dim;
   p.v_pos = v_pos;
   p.inv_tau = static_cast<A>(inv_tau);
+  p.tok = tok;
+  p.bias = bias;
   const size_t budget = static_cast<size_t>(max_smem_optin()) - 2048;
   // a whole row per CTA when it fits (buffers over the row's own reach); time tiles otherwise
   size_t smem = 0;
@@ -868,11 +888,13 @@ int run_forward(int64_t rows, int64_t n, const void* x, const void* h,
 template <typename A>
 int run_pyramid(int64_t rows, int64_t n, const void* x, const fdwt_morlet_plan* pl,
                 const Geometry& g, A* pyr, int64_t pyr_len, const int32_t* pyr_off,
-                cudaStream_t stream) {
+                cudaStream_t stream, int tok = 0, int64_t dim = 1) {
   if (rows == 0 || pl->n_octaves < 2) return FDWT_OK;
   FwdParams<A> p{};
   fill_common(p, pl, g, n);
   p.rows = rows;
+  p.tok = tok;
+  p.dim = dim;
   p.x = x;
   p.pyr = pyr;
   p.pyr_len = pyr_len;

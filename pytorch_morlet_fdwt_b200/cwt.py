@@ -30,7 +30,7 @@ from torch import nn
 from . import _lib
 
 __all__ = ["cwt", "CWT1D", "MorletPlan", "freqs_to_scales", "scales_to_freqs", "morlet_mix",
-           "spectral_softmax"]
+           "morlet_mix_tokens", "spectral_softmax"]
 
 _PI_M14 = math.pi ** -0.25
 _MAX_OCT, _MAX_SCALES, _MAX_LP = 24, 256, 49
@@ -579,6 +579,106 @@ def morlet_mix(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor, a: torch.Tens
     if x2.dtype not in (torch.float32, torch.float64):
         x2 = x2.float()
     return _MorletMixFunction.apply(x2, plan, H, a, b).view(B, D, N)
+
+
+def _mix_tokens_forward(x, plan, H, a, b, bias):
+    dev = _lib.require_cuda(x, H, a, b)
+    lib = _lib.load()
+    B, N, D = x.shape
+    y = torch.empty_like(x)
+    Hd = _filters_on(H, x)
+    a_ = a.detach().to(x.dtype).contiguous()
+    b_ = b.detach().to(x.dtype).contiguous()
+    c_ = None if bias is None else bias.detach().to(x.dtype).contiguous()
+    with torch.cuda.device(dev):
+        st = lib.fdwt_mix_tokens_forward(
+            _lib.dtype_code(x.dtype), B, N, D, x.data_ptr(), Hd.data_ptr(),
+            ctypes.addressof(plan.capi()), a_.data_ptr(), b_.data_ptr(),
+            None if c_ is None else c_.data_ptr(), y.data_ptr(), _lib.stream_of(dev))
+    _lib.check(st, "fdwt_mix_tokens_forward")
+    return y
+
+
+def _mix_tokens_backward(gy, x, plan, H, a, b, need_x, need_h, need_bias):
+    dev = _lib.require_cuda(gy, x, H, a, b)
+    lib = _lib.load()
+    B, N, D = x.shape
+    dt = x.dtype
+    gy = gy.to(dt).contiguous()
+    Hd = _filters_on(H, x)
+    a_ = a.detach().to(dt).contiguous()
+    b_ = b.detach().to(dt).contiguous()
+    gx = torch.empty_like(x) if need_x else None
+    gh = torch.empty_like(Hd) if need_h else None
+    ga = torch.empty_like(a_)
+    gb = torch.empty_like(b_)
+    gc = torch.empty(D, device=dev, dtype=dt) if need_bias else None
+    code = _lib.dtype_code(dt)
+    plan_p = ctypes.addressof(plan.capi())
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    with torch.cuda.device(dev):
+        nws = lib.fdwt_mix_tokens_backward_workspace(code, B, N, D, plan_p, int(need_h))
+        ws = _lib.workspace(nws, dev)
+        st = lib.fdwt_mix_tokens_backward(
+            code, B, N, D, x.data_ptr(), Hd.data_ptr(), plan_p, a_.data_ptr(), b_.data_ptr(),
+            gy.data_ptr(), ptr(gx), ptr(gh), ga.data_ptr(), gb.data_ptr(), ptr(gc), ptr(ws), nws,
+            _lib.stream_of(dev))
+    _lib.check(st, "fdwt_mix_tokens_backward")
+    return gx, gh, ga, gb, gc
+
+
+def _mix_tokens_composed(x, plan, H, a, b, bias):
+    """The token-layout mix through the transform node (higher-order derivatives)."""
+    B, N, D = x.shape
+    y = _mix_composed(x.transpose(1, 2).reshape(B * D, N), plan, H, a, b)
+    y = y.view(B, D, N).transpose(1, 2)
+    return y if bias is None else y + bias.to(y.dtype)
+
+
+class _MorletMixTokensFunction(torch.autograd.Function):
+    """The mix on ``(B, N, D)`` tokens with the bias added: MorletTokenMixer's
+    ``morlet_mix(x.transpose(1, 2), ...).transpose(1, 2) + bias`` (``fdwt/layers.py:49-55``)
+    in one forward kernel and one backward call, without the transposes."""
+
+    @staticmethod
+    def forward(ctx, x, plan: MorletPlan, H, a, b, bias):
+        ctx.plan = plan
+        ctx.has_bias = bias is not None
+        ctx.save_for_backward(x, H, a, b, bias if bias is not None else x.new_zeros(0))
+        return _mix_tokens_forward(x, plan, H, a, b, bias)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, H, a, b, bias = ctx.saved_tensors
+        if not ctx.has_bias:
+            bias = None
+        if torch.is_grad_enabled():
+            if bias is None:
+                return _recomputed_grads(ctx, gy, (x, H, a, b), lambda x_, H_, a_, b_:
+                                         _mix_tokens_composed(x_, ctx.plan, H_, a_, b_, None),
+                                         (0, 2, 3, 4)) + (None,)
+            return _recomputed_grads(ctx, gy, (x, H, a, b, bias), lambda x_, H_, a_, b_, c_:
+                                     _mix_tokens_composed(x_, ctx.plan, H_, a_, b_, c_),
+                                     (0, 2, 3, 4, 5))
+        need_h = ctx.needs_input_grad[2]
+        need_bias = bias is not None and ctx.needs_input_grad[5]
+        gx, gH, ga, gb, gc = _mix_tokens_backward(gy, x, ctx.plan, H, a, b,
+                                                  ctx.needs_input_grad[0], need_h, need_bias)
+        return (gx, None, gH.to(H.dtype) if need_h else None, ga.to(a.dtype), gb.to(b.dtype),
+                gc.to(bias.dtype) if need_bias else None)
+
+
+def morlet_mix_tokens(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor, a: torch.Tensor,
+                      b: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x (B, N, D)`` -> ``sum_s a[d, s] |W_s x[b, :, d]| + b[d, s] Re W_s (+ bias[d])``,
+    shape ``(B, N, D)``: ``morlet_mix`` on the token layout, read and written in place by the
+    kernels (no transposes), with the bias added in the same kernel."""
+    _lib.require_cuda(x)
+    if x.dim() != 3:
+        raise ValueError(f"expected (B, N, D) tokens, got shape {tuple(x.shape)}")
+    dt = torch.float64 if x.dtype == torch.float64 else torch.float32
+    xc = x if x.dtype == dt and x.is_contiguous() else x.to(dt).contiguous()
+    return _MorletMixTokensFunction.apply(xc, plan, H, a, b, bias)
 
 
 def _softmax_forward(x2, plan, H, V, nch, tau):

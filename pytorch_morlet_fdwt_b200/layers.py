@@ -13,7 +13,7 @@ from typing import Optional, Sequence
 import torch
 from torch import nn
 
-from .cwt import CWT1D, morlet_mix, spectral_softmax
+from .cwt import CWT1D, morlet_mix_tokens, spectral_softmax
 from .dwt import wavedec, waverec
 from .wavelets import WaveletLike
 
@@ -49,8 +49,8 @@ class MorletTokenMixer(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = torch.float64 if x.dtype == torch.float64 else torch.float32
         H = self.cwt._filters(x.device, dt)
-        y = morlet_mix(x.transpose(1, 2), self.cwt.plan, H, self.mag_weight, self.phase_weight)
-        y = y.transpose(1, 2) + self.bias
+        # the kernels read the (B, L, D) tokens and write y + bias in the same layout
+        y = morlet_mix_tokens(x, self.cwt.plan, H, self.mag_weight, self.phase_weight, self.bias)
         return self.out_proj(y.to(x.dtype))
 
 
