@@ -1,7 +1,8 @@
-// C ABI of the Morlet CWT pyramid kernels (cwt_impl.cuh).  The computation type follows the
-// row type: fp32 rows compute in fp32, fp64 rows in fp64 (fp16/bf16 inputs are upcast to fp32
-// by the caller, as the reference does at fdwt/cwt.py:606-607).
-#include "cwt_bwd_tiled.cuh"
+// C ABI of the Morlet CWT pyramid kernels (cwt_impl.cuh, cwt_bwd.cuh, cwt_bwd_tiled.cuh).  The
+// computation type follows the row type: fp32 rows compute in fp32, fp64 rows in fp64 (fp16/bf16
+// inputs are upcast to fp32 by the caller, as the reference does at fdwt/cwt.py:606-607).  The
+// kernels are instantiated per (type, epilogue) in cwt_<type>_<epilogue>.cu (cwt_entry.cuh).
+#include "cwt_entry.cuh"
 
 using namespace fdwt;
 using namespace fdwt::cwtk;
@@ -15,11 +16,11 @@ int dispatch_forward(int dtype, int64_t rows, int64_t n, const void* x, const vo
                      cudaStream_t stream, int tok = 0, const void* bias = nullptr) {
   switch (dtype) {
     case FDWT_F32:
-      return run_forward<float, float, EPI>(rows, n, x, h, pl, y, a, b, m, l, dim, v_pos, inv_tau,
-                                            stream, tok, bias);
+      return fwd_entry<float, EPI>(rows, n, x, h, pl, y, a, b, m, l, dim, v_pos, inv_tau, stream,
+                                   tok, bias);
     case FDWT_F64:
-      return run_forward<double, double, EPI>(rows, n, x, h, pl, y, a, b, m, l, dim, v_pos,
-                                              inv_tau, stream, tok, bias);
+      return fwd_entry<double, EPI>(rows, n, x, h, pl, y, a, b, m, l, dim, v_pos, inv_tau,
+                                    stream, tok, bias);
     default:
       return FDWT_ERR_UNSUPPORTED;
   }
@@ -34,11 +35,11 @@ int dispatch_backward(int dtype, int64_t rows, int64_t n, const void* x, const v
                       size_t* need) {
   switch (dtype) {
     case FDWT_F32:
-      return run_backward<float, EPI>(rows, n, x, h, pl, a, b, dim, v_pos, inv_tau, g, m, l, out,
-                                      gx, gh, ga, gb, gv, need_h, ws, ws_bytes, stream, need);
+      return bwd_entry<float, EPI>(rows, n, x, h, pl, a, b, dim, v_pos, inv_tau, g, m, l, out,
+                                   gx, gh, ga, gb, gv, need_h, ws, ws_bytes, stream, need);
     case FDWT_F64:
-      return run_backward<double, EPI>(rows, n, x, h, pl, a, b, dim, v_pos, inv_tau, g, m, l, out,
-                                       gx, gh, ga, gb, gv, need_h, ws, ws_bytes, stream, need);
+      return bwd_entry<double, EPI>(rows, n, x, h, pl, a, b, dim, v_pos, inv_tau, g, m, l, out,
+                                    gx, gh, ga, gb, gv, need_h, ws, ws_bytes, stream, need);
     default:
       return FDWT_ERR_UNSUPPORTED;
   }
@@ -191,11 +192,11 @@ int dispatch_tokens_backward(int dtype, int64_t batch, int64_t n, int64_t dim, c
                              cudaStream_t stream, size_t* need) {
   switch (dtype) {
     case FDWT_F32:
-      return run_mix_tokens_backward<float>(batch, n, dim, x, h, pl, a, b, gy, gx, gh, ga, gb,
-                                            gbias, need_h, ws, ws_bytes, stream, need);
+      return tokens_bwd_entry<float>(batch, n, dim, x, h, pl, a, b, gy, gx, gh, ga, gb, gbias,
+                                     need_h, ws, ws_bytes, stream, need);
     case FDWT_F64:
-      return run_mix_tokens_backward<double>(batch, n, dim, x, h, pl, a, b, gy, gx, gh, ga, gb,
-                                             gbias, need_h, ws, ws_bytes, stream, need);
+      return tokens_bwd_entry<double>(batch, n, dim, x, h, pl, a, b, gy, gx, gh, ga, gb, gbias,
+                                      need_h, ws, ws_bytes, stream, need);
     default:
       return FDWT_ERR_UNSUPPORTED;
   }

@@ -1,6 +1,5 @@
 // Backward of the Morlet CWT pyramid for rows too long for the row-resident kernel
-// (cwt_bwd.cuh): one launch per octave, coarse to fine, over time tiles.  Included by cwt.cu
-// after cwt_bwd.cuh.
+// (cwt_bwd.cuh): one launch per octave, coarse to fine, over time tiles.
 //
 // The chain dL/dx_j = M_j^T dL/dW_j + LP_j^T dL/dx_{j+1} (G_j) is cut at every octave: launch j
 // reads G_{j+1} from global memory, adds the adjoint of its own scales and writes G_j (G_0 is

@@ -1,0 +1,8 @@
+// float instantiation of the Morlet CWT kernels with the softmax epilogue (cwt_entry.cuh).
+#include "cwt_entry.cuh"
+
+namespace fdwt {
+namespace cwtk {
+FDWT_CWT_INSTANTIATE(float, EPI_SOFTMAX)
+}  // namespace cwtk
+}  // namespace fdwt

@@ -1,6 +1,6 @@
 // Morlet CWT octave pyramid for sm_100a: forward transform and the two fused scalogram
 // consumers (magnitude/phase mix, online spectral softmax).  Templates; instantiated per
-// element type in cwt_f32.cu / cwt_f64.cu.
+// element type and epilogue in cwt_<type>_<epilogue>.cu (cwt_entry.cuh).
 //
 // One CTA owns one signal row, or one time tile of a row too long for one CTA's shared memory.
 // The pyramid x_0, x_1, ... lives in two ping-pong shared buffers that cover every position a
