@@ -38,6 +38,13 @@ constexpr int NW_MAX = NTB_MAX / 32;
 __device__ __forceinline__ int nthreads() { return static_cast<int>(blockDim.x); }
 __device__ __forceinline__ int nwarps() { return static_cast<int>(blockDim.x) >> 5; }
 constexpr int KT = 8;        // taps per thread in the filter-gradient reduction
+constexpr int RL = 7;        // positions per lane run of the filter-gradient reduction
+
+// The backward's shared buffers are linear (position q of a buffer reaching e past the row at
+// index q + e).  Work items of P (7) outputs and filter-gradient runs of RL (7) positions are odd
+// in length, so the 32 lanes of a warp, which start P 2^j (or RL 2^j) apart, read distinct banks
+// at every power-of-two dilation 2^j.
+__host__ __device__ __forceinline__ int bix(int e) { return e; }
 
 template <typename A>
 struct BwdParams {
@@ -75,7 +82,7 @@ struct Cplx<double> {
 // ------------------------------------------------------------------------------ buffers
 
 // A shared buffer holding positions [-ext, n + ext) of a row (or of a tile's window): position
-// q at padded index sidx(q + ext).  Reads through ldE are clamped into that range.
+// q at index q + ext.  Reads through ldE are clamped into that range.
 struct Win {
   int n, ext;
 };
@@ -88,11 +95,11 @@ __device__ __forceinline__ int clampE(const Win& w, int pos) {
 }
 template <typename A>
 __device__ __forceinline__ A ldE(const Win& w, const A* buf, int pos) {
-  return buf[sidx<PS>(clampE(w, pos) + w.ext)];
+  return buf[bix(clampE(w, pos) + w.ext)];
 }
 template <typename A>
 __device__ __forceinline__ A& atE(const Win& w, A* buf, int pos) {
-  return buf[sidx<PS>(pos + w.ext)];
+  return buf[bix(pos + w.ext)];
 }
 template <typename A>
 __device__ __forceinline__ A ldE(const FwdParams<A>& f, const A* buf, int pos) {
@@ -106,7 +113,7 @@ __device__ __forceinline__ A& atE(const FwdParams<A>& f, A* buf, int pos) {
 // dL/dW buffer: positions [-1, n] (the two ends stay zero), complex values interleaved.
 template <typename A, int C>
 __device__ __forceinline__ typename Cplx<A>::type ld_gw(const A* gw, int n, int pos) {
-  const int q = sidx<PS>(min(max(pos, -1), n) + 1);
+  const int q = bix(min(max(pos, -1), n) + 1);
   typename Cplx<A>::type v;
   if (C == 2) {
     v = *reinterpret_cast<const typename Cplx<A>::type*>(gw + 2 * q);
@@ -119,7 +126,7 @@ __device__ __forceinline__ typename Cplx<A>::type ld_gw(const A* gw, int n, int 
 // The same without the clamp, for positions known to lie in [-1, n].
 template <typename A, int C>
 __device__ __forceinline__ typename Cplx<A>::type ld_gw_in(const A* gw, int pos) {
-  const int q = sidx<PS>(pos + 1);
+  const int q = bix(pos + 1);
   typename Cplx<A>::type v;
   if (C == 2) {
     v = *reinterpret_cast<const typename Cplx<A>::type*>(gw + 2 * q);
@@ -135,12 +142,12 @@ __device__ __forceinline__ typename Cplx<A>::type ld_gw_sel(const A* gw, int n, 
 }
 template <typename A, bool CLAMP>
 __device__ __forceinline__ A ldE_sel(const FwdParams<A>& f, const A* buf, int pos) {
-  return CLAMP ? ldE(f, buf, pos) : buf[sidx<PS>(pos + f.ext)];
+  return CLAMP ? ldE(f, buf, pos) : buf[bix(pos + f.ext)];
 }
 
 template <typename A, int C>
 __device__ __forceinline__ void st_gw(A* gw, int pos, A re, A im) {
-  const int q = sidx<PS>(pos + 1);
+  const int q = bix(pos + 1);
   if (C == 2) {
     gw[2 * q] = re;
     gw[2 * q + 1] = im;
@@ -202,7 +209,7 @@ __device__ __forceinline__ void stage_gw(const BwdParams<A>& p, int gs, int64_t 
   const A* g = p.g + (row * p.f.n_scales + gs) * p.f.n * C;
   constexpr int bytes = static_cast<int>(sizeof(A)) * C;
   for (int q = threadIdx.x; q < n; q += nthreads()) {
-    A* d = C == 2 ? gw + 2 * sidx<PS>(q + 1) : gw + sidx<PS>(q + 1);
+    A* d = C == 2 ? gw + 2 * bix(q + 1) : gw + bix(q + 1);
     const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(d));
     const A* src = g + static_cast<int64_t>(q) * C;
     if (bytes == 16)
@@ -264,7 +271,7 @@ __device__ void bwd_lowpass_adjoint(const FwdParams<A>& f, const A* src, A* dst,
 template <typename A, bool SYM, bool CLAMP = true>
 __device__ __forceinline__ void conv_one(const Win& f, const A* X, const A* tab, int K,
                                          int dil, int base, Acc2<A> (&acc)[P]) {
-  auto ld = [&](int pos) { return CLAMP ? ldE(f, X, pos) : X[sidx<PS>(pos + f.ext)]; };
+  auto ld = [&](int pos) { return CLAMP ? ldE(f, X, pos) : X[bix(pos + f.ext)]; };
   A L[P], R[P];
 #pragma unroll
   for (int i = 0; i < P; ++i) L[i] = R[i] = ld(base + dil * i);
@@ -378,17 +385,17 @@ __device__ void adjoint_scale(const Win& f, const Oct& O, const A* tab, const A*
   }
 }
 
-// One run of gradh_scale: 8 positions nn + dil*t against the taps k0 .. k0 + 7 (base = nn - dil k0).
+// One run of gradh_scale: RL positions nn + dil*t against the taps k0 .. k0 + 7 (base = nn - dil k0).
 template <typename A, int C, bool CLAMP>
 __device__ __forceinline__ void gradh_run(const FwdParams<A>& f, const A* X, const A* gw, int n,
                                           int dil, int nn, int base, Acc2<A> (&acc)[KT]) {
   using V2 = typename Cplx<A>::type;
-  A xw[2 * KT - 1];  // x_j(base + dil*(m - 7)), m = 0..14
+  A xw[RL + KT - 1];  // x_j(base + dil*(m - 7)), m = 0..13
 #pragma unroll
-  for (int m = 0; m < 2 * KT - 1; ++m)
+  for (int m = 0; m < RL + KT - 1; ++m)
     xw[m] = ldE_sel<A, CLAMP>(f, X, base + dil * (m - (KT - 1)));
 #pragma unroll
-  for (int t = 0; t < KT; ++t) {
+  for (int t = 0; t < RL; ++t) {
     const V2 gv = ld_gw_sel<A, C, CLAMP>(gw, n, nn + dil * t);
 #pragma unroll
     for (int i = 0; i < KT; ++i) {
@@ -400,14 +407,14 @@ __device__ __forceinline__ void gradh_run(const FwdParams<A>& f, const A* X, con
 
 // Per-row dL/dH of one scale: part[c*hcols + center + k] = sum_n gW_c(n) x_j(n - dil k) for
 // |k| <= K (zero elsewhere).  Warp w reduces taps [k0, k0 + KT) for kb = w, w + NW, ...; its lanes
-// take runs of 8 positions n = nn + dil*t of one phase (runs ordered phase-minor, so that the
-// lanes of a warp read distinct banks), load the run's 15-value window of x_j and its 8 dL/dW
-// pairs once, and accumulate 8 x 8 packed products.  Positions past the row end read the zero
+// take runs of RL positions n = nn + dil*t of one phase (runs ordered phase-minor, so that the
+// lanes of a warp read distinct banks), load the run's 14-value window of x_j and its 7 dL/dW
+// pairs once, and accumulate 7 x 8 packed products.  Positions past the row end read the zero
 // cells of the dL/dW buffer.  Lane partials are summed with shuffles.
 template <typename A, int C>
 __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, const A* gw,
                             A* part) {
-  static_assert(KT == 8, "a run is 8 positions");
+
   const int n = static_cast<int>(f.n);
   const int dil = O.dil, K = O.half;
   const int lg = __ffs(dil) - 1;  // dil = 2^lg
@@ -415,7 +422,7 @@ __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, con
   const int ntap = 2 * K + 1;
   const int nkb = static_cast<int>(cdiv(ntap, KT));
   const int U = static_cast<int>(cdiv(n, dil));
-  const int runs = dil * ((U + 7) >> 3);
+  const int runs = dil * ((U + RL - 1) / RL);
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   using V2 = typename Cplx<A>::type;
   for (int c = threadIdx.x; c < C * hcols; c += nthreads()) {
@@ -428,11 +435,11 @@ __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, con
 #pragma unroll
     for (int i = 0; i < KT; ++i) acc[i].zero();
     for (int r = lane; r < runs; r += 32) {
-      const int nn = (r & (dil - 1)) + ((r >> lg) << (lg + 3));  // phase + dil * 8 * run
+      const int nn = (r & (dil - 1)) + (r >> lg) * (RL << lg);  // phase + dil * RL * run
       if (nn >= n) continue;
       const int base = nn - dil * k0;
       const bool inside = base - dil * (KT - 1) >= -f.ext &&
-                          base + dil * (KT - 1) <= n + f.ext - 1 && nn + dil * (KT - 1) <= n;
+                          base + dil * (RL - 1) <= n + f.ext - 1 && nn + dil * (RL - 1) <= n;
       if (inside) gradh_run<A, C, false>(f, X, gw, n, dil, nn, base, acc);
       else gradh_run<A, C, true>(f, X, gw, n, dil, nn, base, acc);
     }
@@ -800,8 +807,8 @@ BwdLayout bwd_layout(int EPI, int64_t rows, int64_t n, const fdwt_morlet_plan* p
 // into p when it is given).
 template <typename A, int EPI>
 size_t row_bwd_smem(int64_t n, const fdwt_morlet_plan* pl, int ext, BwdParams<A>* p) {
-  const int64_t buf_len = padded_len<PS>(n + 2 * static_cast<int64_t>(ext)) + 8;
-  const int64_t gw_len = 2 * padded_len<PS>(n + 2) + 8;
+  const int64_t buf_len = (n + 2 * static_cast<int64_t>(ext)) + 8;
+  const int64_t gw_len = 2 * (n + 2) + 8;
   if (buf_len > 0x3fffffffLL) return ~size_t(0);
   size_t off = 3 * static_cast<size_t>(buf_len) * sizeof(A);
   off = (off + 15) / 16 * 16;

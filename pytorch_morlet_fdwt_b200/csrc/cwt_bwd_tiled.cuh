@@ -43,7 +43,7 @@ struct OctParams {
 
 // dL/dH partial of one scale over the owned positions [lo, hi) (absolute):
 // part[c * hcols + center + k] = sum_a gW_c(a) x_j(a - dil k), |k| <= K, zero elsewhere.  Same
-// reduction as gradh_scale (runs of 8 positions of a phase per lane, 8 taps per warp pass); gW
+// reduction as gradh_scale (runs of RL positions of a phase per lane, 8 taps per warp pass); gW
 // is read from its window (origin o, virtual length nv) and counts only inside [lo, hi).
 template <typename A, int C>
 __device__ void gradh_tile(const Oct& O, int center, const A* X, int xorg, int xlen,
@@ -54,7 +54,7 @@ __device__ void gradh_tile(const Oct& O, int center, const A* X, int xorg, int x
   const int nkb = static_cast<int>(cdiv(2 * K + 1, KT));
   const int len = max(hi - lo, 0);
   const int U = static_cast<int>(cdiv(len, dil));
-  const int runs = dil * ((U + 7) >> 3);
+  const int runs = dil * ((U + RL - 1) / RL);
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   using V2 = typename Cplx<A>::type;
   for (int c = threadIdx.x; c < C * hcols; c += nthreads()) {
@@ -67,17 +67,17 @@ __device__ void gradh_tile(const Oct& O, int center, const A* X, int xorg, int x
 #pragma unroll
     for (int i = 0; i < KT; ++i) acc[i].zero();
     for (int r = lane; r < runs; r += 32) {
-      const int nn = lo + (r & (dil - 1)) + ((r >> lg) << (lg + 3));  // phase + dil * 8 * run
+      const int nn = lo + (r & (dil - 1)) + (r >> lg) * (RL << lg);  // phase + dil RL run
       if (nn >= hi) continue;
       const int base = nn - dil * k0;
-      A xw[2 * KT - 1];  // x_j(base + dil (m - 7)); taps past K read clamped cells (discarded)
+      A xw[RL + KT - 1];  // x_j(base + dil (m - 7)); taps past K read clamped cells (discarded)
 #pragma unroll
-      for (int m = 0; m < 2 * KT - 1; ++m) {
+      for (int m = 0; m < RL + KT - 1; ++m) {
         const int i = min(max(base + dil * (m - (KT - 1)) - xorg, 0), xlen - 1);
-        xw[m] = X[sidx<PS>(i)];
+        xw[m] = X[bix(i)];
       }
 #pragma unroll
-      for (int t = 0; t < KT; ++t) {
+      for (int t = 0; t < RL; ++t) {
         const int a = nn + dil * t;
         V2 gv = ld_gw<A, C>(gw, nv, a - o);
         if (a >= hi) {
@@ -281,14 +281,14 @@ __global__ void __launch_bounds__(NT) cwt_octave_bwd_kernel(const __grid_constan
                  : RowRef<const A>{p.pyr + row * p.pyr_len + p.pyr_off[q.j] + live, 1};
     for (int i = tid; i < tk + 2 * q.XH; i += nthreads()) {
       const int a = t0 - q.XH + i;
-      X[sidx<PS>(i)] = (a >= -live && a < n + live) ? src[a] : A(0);
+      X[bix(i)] = (a >= -live && a < n + live) ? src[a] : A(0);
     }
   }
   if (has_in) {
     const A* gi = q.g_in + row * q.g_stride + q.e;
     for (int i = tid; i < tk + 2 * q.R; i += nthreads()) {
       const int a = t0 - q.R + i;
-      Gp[sidx<PS>(i)] = (a >= -q.e && a < n + q.e) ? gi[a] : A(0);
+      Gp[bix(i)] = (a >= -q.e && a < n + q.e) ? gi[a] : A(0);
     }
   }
   for (int i = tid; i < q.gw_len; i += nthreads()) gw[i] = A(0);  // the window's end cells stay zero
@@ -299,14 +299,14 @@ __global__ void __launch_bounds__(NT) cwt_octave_bwd_kernel(const __grid_constan
       A v = A(0);
       if (has_in && a >= -live && a < n + live) {
         const int c = i + q.R;
-        v = f.lpp[0] * Gp[sidx<PS>(c)];
+        v = f.lpp[0] * Gp[bix(c)];
         for (int k = 0; k < f.n_lp; ++k) {
           const int t = f.lp_t[k];
-          v = fma(f.lp_p[k], Gp[sidx<PS>(c + dil * t)], v);
-          v = fma(f.lp_m[k], Gp[sidx<PS>(c - dil * t)], v);
+          v = fma(f.lp_p[k], Gp[bix(c + dil * t)], v);
+          v = fma(f.lp_m[k], Gp[bix(c - dil * t)], v);
         }
       }
-      Go[sidx<PS>(i)] = v;
+      Go[bix(i)] = v;
     }
   }
   if (O.count > 0) {
@@ -323,13 +323,13 @@ __global__ void __launch_bounds__(NT) cwt_octave_bwd_kernel(const __grid_constan
       A* go = q.g_out + row * q.g_stride + q.e;
       for (int i = tid; i < tk; i += nthreads()) {
         const int a = t0 + i;
-        if (a < n + q.e) go[a] = Go[sidx<PS>(i)];
+        if (a < n + q.e) go[a] = Go[bix(i)];
       }
     } else {
       const RowRef<A> gx = row_ref(p.gx, f, row);
       for (int i = tid; i < tk; i += nthreads()) {
         const int a = t0 + i;
-        if (a >= 0 && a < n) gx[a] = Go[sidx<PS>(i)];
+        if (a >= 0 && a < n) gx[a] = Go[bix(i)];
       }
     }
   }
@@ -357,11 +357,11 @@ size_t oct_layout(OctParams<A>& q, const fdwt_morlet_plan* pl, int j, int t_len,
     return static_cast<int32_t>(at);
   };
   q.x_off = region(q.XH > 0 || (need_x && cnt > 0)
-                       ? static_cast<size_t>(padded_len<PS>(t_len + 2 * q.XH)) + 8 : 0);
-  q.gw_len = cnt > 0 ? static_cast<int32_t>(C * padded_len<PS>(nv + 2) + 8) : 0;
+                       ? static_cast<size_t>((t_len + 2 * q.XH)) + 8 : 0);
+  q.gw_len = cnt > 0 ? static_cast<int32_t>(C * (nv + 2) + 8) : 0;
   q.gw_off = region(q.gw_len);
-  q.gp_off = region(q.R > 0 ? static_cast<size_t>(padded_len<PS>(t_len + 2 * q.R)) + 8 : 0);
-  q.go_off = region(need_gx ? static_cast<size_t>(padded_len<PS>(t_len)) + 8 : 0);
+  q.gp_off = region(q.R > 0 ? static_cast<size_t>((t_len + 2 * q.R)) + 8 : 0);
+  q.go_off = region(need_gx ? static_cast<size_t>((t_len)) + 8 : 0);
   q.tab_off = region(4 * static_cast<size_t>(cnt) * (pl->oct_half[j] + 1));
   q.red_off = region(NW_MAX);
   const size_t smem = off + 16;

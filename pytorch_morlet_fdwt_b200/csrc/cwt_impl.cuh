@@ -52,7 +52,8 @@ namespace fdwt {
 namespace cwtk {
 
 constexpr int NT = 256;           // threads per CTA
-constexpr int P = 8;              // consecutive polyphase outputs per work item (backward)
+constexpr int P = 7;              // consecutive polyphase outputs per work item (backward):
+                                  // odd, like PF below, for the backward's linear buffers
 constexpr int PF = 5;             // the same in the forward: an odd run length keeps the
                                   // windows of a warp's lanes on distinct banks of the linear
                                   // (unpadded) buffers for every power-of-two dilation
@@ -119,8 +120,8 @@ struct RowRef {
   int64_t step;
   __device__ __forceinline__ T& operator[](int64_t q) const { return p[q * step]; }
 };
-template <typename T, typename P>
-__device__ __forceinline__ RowRef<T> row_ref(T* base, const P& f, int64_t row) {
+template <typename T, typename Prm>
+__device__ __forceinline__ RowRef<T> row_ref(T* base, const Prm& f, int64_t row) {
   if (f.tok) return RowRef<T>{base + (row / f.dim) * f.n * f.dim + row % f.dim, f.dim};
   return RowRef<T>{base + row * f.n, 1};
 }
