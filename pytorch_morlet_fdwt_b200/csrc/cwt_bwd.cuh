@@ -460,6 +460,62 @@ __device__ void gradh_scale(const FwdParams<A>& f, const Oct& O, const A* X, con
   }
 }
 
+// dL/dW at one position from the recomputed W = (re, im) and the upstream gradient go of the
+// consumer (MIX: y = sum a |W| + b Re W; SOFTMAX: out = sum pr V, pr = softmax(|W| tau^-1)
+// with the forward's running max m and denominator l at rq).  The parameter sums go to sa / sb
+// (or, for a per-position V, to *vpos) when `own`.  fp32 takes |W| and 1/|W| from one
+// reciprocal square root and the softmax weight from the fast exponential and division
+// (rsqrtf, __expf, __fdividef: a few ulp, l >= 1); fp64 uses exact operations.
+template <typename A, int EPI, int C>
+__device__ __forceinline__ void consumer_grad(const BwdParams<A>& p, A re, A im, A go, A av,
+                                              A bv, A vv, int64_t rq, A* vpos, bool own,
+                                              A& sa, A& sb, A& gre, A& gim) {
+  constexpr bool F32 = std::is_same<A, float>::value;
+  A mag, rs = A(0);
+  if (C == 2) {
+    if constexpr (F32) {
+      const float s2 = fmaf(re, re, im * im);
+      rs = s2 > 0.0f ? rsqrtf(s2) : 0.0f;
+      mag = s2 * rs;
+    } else {
+      mag = sqrt(re * re + im * im);
+      rs = mag > A(0) ? A(1) / mag : A(0);
+    }
+  } else {
+    mag = fabs(re);
+  }
+  if (EPI == EPI_MIX) {
+    if (own) {
+      sa += go * mag;
+      sb += go * re;
+    }
+    if (C == 2) {
+      const A r = av * go * rs;
+      gre = r * re + bv * go;
+      gim = r * im;
+    } else {
+      const A sg = re > A(0) ? A(1) : (re < A(0) ? A(-1) : A(0));
+      gre = go * (av * sg + bv);
+      gim = A(0);
+    }
+  } else {
+    const A inv_tau = p.f.inv_tau;
+    A w;  // pr * go
+    if constexpr (F32)
+      w = __fdividef(__expf(fmaf(mag, inv_tau, -p.sm_m[rq])) * go, p.sm_l[rq]);
+    else
+      w = exp(mag * inv_tau - p.sm_m[rq]) / p.sm_l[rq] * go;
+    const A gmag = w * (vv - p.sm_out[rq]) * inv_tau;
+    if (own) {
+      if (vpos) atomicAdd(vpos, w);
+      else sa += w;
+    }
+    const A r = gmag * rs;
+    gre = r * re;
+    gim = r * im;
+  }
+}
+
 // dL/dW_s on [0, n) into the gW buffer.  STORE: copied from the caller's gradient.  MIX /
 // SOFTMAX: W_s is recomputed from x_j and the epilogue's derivative applied; the per-row
 // parameter partials are returned through *pa_sum, *pb_sum (thread-local, summed by caller).
@@ -511,34 +567,16 @@ __device__ void make_gw(const BwdParams<A>& p, const Oct& O, int s, int gs, cons
       const int q = base + dil * i;
       if (q >= n) continue;
       const A re = acc[i].re(), im = C == 2 ? acc[i].im() : A(0);
-      const A mag = C == 2 ? sqrt(re * re + im * im) : fabs(re);
-      const A go = gy[q];
-      A gre, gim;
-      if (EPI == EPI_MIX) {
-        sa += go * mag;
-        sb += go * re;
-        if (C == 2) {
-          const A r = mag > A(0) ? av * go / mag : A(0);
-          gre = r * re + bv * go;
-          gim = r * im;
-        } else {
-          const A sg = re > A(0) ? A(1) : (re < A(0) ? A(-1) : A(0));
-          gre = go * (av * sg + bv);
-          gim = A(0);
-        }
-      } else {
-        const int64_t rq = row * f.n + q;
-        const A a = mag * f.inv_tau;
-        const A pr = exp(a - p.sm_m[rq]) / p.sm_l[rq];
-        const A v = f.v_pos ? static_cast<const A*>(f.a)[(grp * f.n_scales + gs) * f.n + q]
-                            : vconst;
-        const A gmag = pr * (v - p.sm_out[rq]) * go * f.inv_tau;
-        if (f.v_pos) atomicAdd(p.v_part + (grp * f.n_scales + gs) * f.n + q, pr * go);
-        else sa += pr * go;
-        const A r = mag > A(0) ? gmag / mag : A(0);
-        gre = r * re;
-        gim = r * im;
+      A vv = vconst;
+      A* vpos = nullptr;
+      if (EPI == EPI_SOFTMAX && f.v_pos) {
+        const int64_t vq = (grp * f.n_scales + gs) * f.n + q;
+        vv = static_cast<const A*>(f.a)[vq];
+        vpos = p.v_part + vq;
       }
+      A gre, gim;
+      consumer_grad<A, EPI, C>(p, re, im, gy[q], av, bv, vv, row * f.n + q, vpos, true, sa, sb,
+                               gre, gim);
       st_gw<A, C>(gw, q, gre, gim);
     }
   }

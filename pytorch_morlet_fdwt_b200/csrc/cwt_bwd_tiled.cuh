@@ -163,38 +163,16 @@ __device__ void make_gw_tile(const BwdParams<A>& p, const Oct& O, int gs, const 
       }
       const bool own = a >= lo && a < hi;
       const A re = acc[i].re(), im = C == 2 ? acc[i].im() : A(0);
-      const A mag = C == 2 ? sqrt(re * re + im * im) : fabs(re);
-      const A go = gy[a];
-      A gre, gim;
-      if (EPI == EPI_MIX) {
-        if (own) {
-          sa += go * mag;
-          sb += go * re;
-        }
-        if (C == 2) {
-          const A r = mag > A(0) ? av * go / mag : A(0);
-          gre = r * re + bv * go;
-          gim = r * im;
-        } else {
-          const A sg = re > A(0) ? A(1) : (re < A(0) ? A(-1) : A(0));
-          gre = go * (av * sg + bv);
-          gim = A(0);
-        }
-      } else {
-        const int64_t rq = row * f.n + a;
-        const A am = mag * f.inv_tau;
-        const A pr = exp(am - p.sm_m[rq]) / p.sm_l[rq];
-        const A vv = f.v_pos ? static_cast<const A*>(f.a)[(grp * f.n_scales + gs) * f.n + a]
-                             : vconst;
-        const A gmag = pr * (vv - p.sm_out[rq]) * go * f.inv_tau;
-        if (own) {
-          if (f.v_pos) atomicAdd(p.v_part + (grp * f.n_scales + gs) * f.n + a, pr * go);
-          else sa += pr * go;
-        }
-        const A r = mag > A(0) ? gmag / mag : A(0);
-        gre = r * re;
-        gim = r * im;
+      A vv = vconst;
+      A* vpos = nullptr;
+      if (EPI == EPI_SOFTMAX && f.v_pos) {
+        const int64_t vq = (grp * f.n_scales + gs) * f.n + a;
+        vv = static_cast<const A*>(f.a)[vq];
+        vpos = p.v_part + vq;
       }
+      A gre, gim;
+      consumer_grad<A, EPI, C>(p, re, im, gy[a], av, bv, vv, row * f.n + a, vpos, own, sa, sb,
+                               gre, gim);
       st_gw<A, C>(gw, v, gre, gim);
     }
   }

@@ -182,6 +182,17 @@ struct Acc2<double> {
   __device__ __forceinline__ double im() const { return i; }
 };
 
+// |W| of a complex value: fp32 through one reciprocal square root (rsqrtf, a few ulp), fp64
+// exact.
+__device__ __forceinline__ float cabs_w(float re, float im) {
+  const float s2 = fmaf(re, re, im * im);
+  return s2 > 0.0f ? s2 * rsqrtf(s2) : 0.0f;
+}
+__device__ __forceinline__ double cabs_w(double re, double im) { return sqrt(re * re + im * im); }
+// exp(x) for the softmax weights (x <= 0): fp32 the fast exponential, fp64 exact.
+__device__ __forceinline__ float exp_w(float x) { return __expf(x); }
+__device__ __forceinline__ double exp_w(double x) { return exp(x); }
+
 // Partition of an octave's `count` scales into blocks of 1..4 (each block shares the pair
 // sums of its tap loop).
 __device__ __forceinline__ int block_size(int rem) {
@@ -425,7 +436,7 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
 #pragma unroll
       for (int i = 0; i < PF; ++i) {
         const A re = acc[s][i].re(), im = acc[s][i].im();
-        const A mag = C == 2 ? sqrt(re * re + im * im) : fabs(re);
+        const A mag = C == 2 ? cabs_w(re, im) : fabs(re);
         mix[i] += av * mag + bv * re;
       }
     } else {
@@ -435,16 +446,21 @@ __device__ __forceinline__ void do_block(const FwdParams<A>& p, const Oct& O, co
       for (int i = 0; i < PF; ++i) {
         const int64_t ni = phi + static_cast<int64_t>(dil) * (u0 + i);
         const A re = acc[s][i].re(), im = acc[s][i].im();
-        const A a = sqrt(re * re + im * im) * p.inv_tau;
+        const A a = cabs_w(re, im) * p.inv_tau;
         A v;
         if (p.v_pos) v = ni < tend ? V[(g * p.n_scales + gs) * n + ni] : A(0);
         else v = V[c * p.n_scales + gs];
-        const A m_new = fmax(sm_m[i], a);
-        const A alpha = exp(sm_m[i] - m_new);
-        const A e = exp(a - m_new);
-        sm_l[i] = sm_l[i] * alpha + e;
-        sm_num[i] = sm_num[i] * alpha + e * v;
-        sm_m[i] = m_new;
+        // online softmax: one exponential, of -|a - m| (the larger side's weight is exactly 1)
+        const A dlt = a - sm_m[i];
+        const A ex = exp_w(-fabs(dlt));
+        if (dlt > A(0)) {
+          sm_l[i] = sm_l[i] * ex + A(1);
+          sm_num[i] = sm_num[i] * ex + v;
+          sm_m[i] = a;
+        } else {
+          sm_l[i] = sm_l[i] + ex;
+          sm_num[i] = sm_num[i] + ex * v;
+        }
       }
     }
   }
