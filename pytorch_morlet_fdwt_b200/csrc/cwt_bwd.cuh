@@ -66,6 +66,7 @@ struct BwdParams {
   int32_t need_x;     // pass 2 reads x_j (filter gradient, or recomputation of W)
   int32_t gw_len;     // elements of the dL/dW buffer
   int32_t gw_off, tab_off, red_off;  // byte offsets of the dL/dW buffer, tap table, reduce slots
+  int32_t pipe;       // MIX / SOFTMAX: scales pipelined over two dL/dW buffers (octave_pass)
 };
 
 template <typename A>
@@ -647,10 +648,59 @@ __device__ void octave_pass(const BwdParams<A>& p, const Oct& O, int live, A* G,
       if (sy) scale_grads<A, C, true>(p, O, live, gs, G, X, gws[s & 1], ts, row, ks);
       else scale_grads<A, C, false>(p, O, live, gs, G, X, gws[s & 1], ts, row, ks);
       __syncthreads();
-    } else {
+    } else if (!p.pipe) {
       if (sy) scale_pass<A, EPI, C, true>(p, O, live, s, G, X, gws[0], ts, red, row, ks);
       else scale_pass<A, EPI, C, false>(p, O, live, s, G, X, gws[0], ts, red, row, ks);
     }
+  }
+  if (EPI == EPI_STORE || !p.pipe) return;
+  // MIX / SOFTMAX, pipelined: step t recomputes scale t and forms its dL/dW in gws[t & 1] while
+  // the adjoint and filter gradient of scale t - 1 run from gws[(t - 1) & 1], with one barrier
+  // per step.  The parameter sums of scale t go per warp into slot t & 1 of red + NW_MAX (two
+  // sums x NW_MAX warps) and thread 0 adds them up in warp order at the next step.
+  const FwdParams<A>& f = p.f;
+  A* wsum = red + NW_MAX;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = 0; t <= O.count; ++t) {
+    if (t > 0 && threadIdx.x == 0 && (EPI == EPI_MIX || !f.v_pos)) {
+      const A* ws = wsum + ((t - 1) & 1) * 2 * NW_MAX;
+      A ta = A(0), tb = A(0);
+      for (int i = 0; i < nwarps(); ++i) {
+        ta += ws[i];
+        tb += ws[NW_MAX + i];
+      }
+      const int64_t at = row * f.n_scales + f.order[O.begin + t - 1];
+      if (EPI == EPI_MIX) {
+        p.a_part[at] = ta;
+        p.b_part[at] = tb;
+      } else {
+        p.v_part[at] = ta;
+      }
+    }
+    if (t < O.count) {
+      const int gs = f.order[O.begin + t];
+      const A* ts = tab + 4 * K1 * t;
+      A sa = A(0), sb = A(0);
+      if (sym[t]) make_gw<A, EPI, C, true>(p, O, t, gs, X, ts, klast[t], gws[t & 1], row, sa, sb);
+      else make_gw<A, EPI, C, false>(p, O, t, gs, X, ts, klast[t], gws[t & 1], row, sa, sb);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sa += __shfl_xor_sync(0xffffffffu, sa, o);
+        sb += __shfl_xor_sync(0xffffffffu, sb, o);
+      }
+      if (lane == 0) {
+        wsum[(t & 1) * 2 * NW_MAX + w] = sa;
+        wsum[(t & 1) * 2 * NW_MAX + NW_MAX + w] = sb;
+      }
+    }
+    if (t > 0) {
+      const int s = t - 1;
+      const int gs = f.order[O.begin + s];
+      const A* ts = tab + 4 * K1 * s;
+      if (sym[s]) scale_grads<A, C, true>(p, O, live, gs, G, X, gws[s & 1], ts, row, klast[s]);
+      else scale_grads<A, C, false>(p, O, live, gs, G, X, gws[s & 1], ts, row, klast[s]);
+    }
+    __syncthreads();
   }
 }
 
@@ -673,7 +723,8 @@ __global__ void __launch_bounds__(NTB_MAX) cwt_backward_kernel(const __grid_cons
   const RowRef<const A> xr = row_ref(static_cast<const A*>(f.x), f, row);
 
   // the end cells of the dL/dW buffers (positions -1 and n) are never written again
-  for (int q = threadIdx.x; q < (EPI == EPI_STORE ? 2 : 1) * p.gw_len; q += nthreads()) gws[0][q] = A(0);
+  for (int q = threadIdx.x; q < (EPI == EPI_STORE || p.pipe ? 2 : 1) * p.gw_len; q += nthreads())
+    gws[0][q] = A(0);
   __syncthreads();
 
   // pass 1: x_1 .. x_{J-1} into the row's scratch
@@ -844,14 +895,15 @@ BwdLayout bwd_layout(int EPI, int64_t rows, int64_t n, const fdwt_morlet_plan* p
 // Shared bytes of the row-resident backward kernel for rows of n samples (the buffer offsets go
 // into p when it is given).
 template <typename A, int EPI>
-size_t row_bwd_smem(int64_t n, const fdwt_morlet_plan* pl, int ext, BwdParams<A>* p) {
+size_t row_bwd_smem(int64_t n, const fdwt_morlet_plan* pl, int ext, BwdParams<A>* p,
+                    bool pipe = false) {
   const int64_t buf_len = (n + 2 * static_cast<int64_t>(ext)) + 8;
   const int64_t gw_len = 2 * (n + 2) + 8;
   if (buf_len > 0x3fffffffLL) return ~size_t(0);
   size_t off = 3 * static_cast<size_t>(buf_len) * sizeof(A);
   off = (off + 15) / 16 * 16;
   const size_t gw_off = off;
-  off += (EPI == EPI_STORE ? 2 : 1) * static_cast<size_t>(gw_len) * sizeof(A);
+  off += (EPI == EPI_STORE || pipe ? 2 : 1) * static_cast<size_t>(gw_len) * sizeof(A);
   off = (off + 15) / 16 * 16;
   const size_t tab_off = off;
   size_t tab = 0;  // the largest octave's tap tables
@@ -860,13 +912,14 @@ size_t row_bwd_smem(int64_t n, const fdwt_morlet_plan* pl, int ext, BwdParams<A>
   off += tab * sizeof(A);
   off = (off + 15) / 16 * 16;
   const size_t red_off = off;
-  off += NW_MAX * sizeof(A);
+  off += 5 * NW_MAX * sizeof(A);  // block sums, then the pipelined steps' per-warp sums
   if (p) {
     p->f.buf_len = static_cast<int>(buf_len);
     p->gw_len = static_cast<int>(gw_len);
     p->gw_off = static_cast<int>(gw_off);
     p->tab_off = static_cast<int>(tab_off);
     p->red_off = static_cast<int>(red_off);
+    p->pipe = pipe ? 1 : 0;
   }
   return off + 16;
 }
@@ -977,7 +1030,11 @@ int run_backward(int64_t rows, int64_t n, const void* x, const void* h,
   for (int j = 0; j < kMaxOct; ++j) p.pyr_off[j] = lay.pyr_off[j];
   p.need_gx = gx != nullptr;
   p.need_x = (gh != nullptr || EPI != EPI_STORE) ? 1 : 0;
-  const size_t smem = row_bwd_smem<A, EPI>(n, pl, p.f.ext, &p);
+  size_t smem = row_bwd_smem<A, EPI>(n, pl, p.f.ext, &p);
+  // rows that already take one CTA per SM pipeline their scales when a second dL/dW buffer fits
+  if (EPI != EPI_STORE && smem > budget / 2 &&
+      row_bwd_smem<A, EPI>(n, pl, p.f.ext, nullptr, true) <= budget)
+    smem = row_bwd_smem<A, EPI>(n, pl, p.f.ext, &p, true);
   if (smem > budget) return FDWT_ERR_UNSUPPORTED;
   if (!p.need_gx && gh == nullptr && EPI == EPI_STORE) return FDWT_OK;
   auto kern = cwt_backward_kernel<A, EPI>;
