@@ -356,6 +356,7 @@ class Cfg2(Workload):
 
 class Cfg1(Workload):
     key = "cfg1"
+    graph = True  # launch-bound: also timed as a CUDA-graph replay
     batch = 32
     shape = (64, 2500)
     name = ("cfg1: db4 symmetric level-5 wavedec, its backward of sum(coeffs^2), and waverec, "
@@ -724,6 +725,44 @@ def time_steps(W, st, steps, warmup, world, dev, barrier):
     return ms, fwd, bwd, launches
 
 
+def time_graph(W, st, steps, world, dev, barrier):
+    """The fwd+bwd step captured once in a CUDA graph (torch.cuda.graph) and replayed `steps`
+    times: device ms (max over ranks) and this library's launches per replayed step (counted
+    while capturing).  For launch-bound shapes, where the eager step measures the host."""
+    import torch
+    from pytorch_morlet_fdwt_b200 import _lib
+    for k in ("c", "y"):  # drop the eager steps' autograd graphs (their AccumulateGrad nodes)
+        st.pop(k, None)
+    st["x"].grad = None
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            W.fwd(st)
+            W.bwd(st)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    l0 = _lib.launch_count()
+    with torch.cuda.graph(g):
+        W.fwd(st)
+        W.bwd(st)
+    per_step = _lib.launch_count() - l0
+    g.replay()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    (ms,) = max_over_ranks([e0.elapsed_time(e1)], world, dev)
+    del g
+    return ms, per_step
+
+
 def time_call(fn, reps, barrier):
     """Mean device time (ms) of one call of fn over `reps` back-to-back calls, and the number of
     this library's launches per call."""
@@ -821,6 +860,21 @@ def measure_config(W, args, world, dev, barrier, cpu, fp32_peak, batch=None, ful
            "ms_per_step": round(ms / steps, 4), "fwd_ms": round(fwd, 4),
            "bwd_ms": round(bwd, 4), "gpu_launches": int(launches),
            "units_per_step_per_gpu": units}
+    if getattr(W, "graph", False):
+        try:
+            g_ms, g_launches = time_graph(W, st, steps, world, dev, barrier)
+        except RuntimeError as e:  # capture refused: report it, keep the eager numbers
+            g_ms, g_launches = None, repr(e)[:200]
+    if getattr(W, "graph", False) and g_ms is None:
+        out["graph_replay"] = {"unavailable": g_launches}
+    elif getattr(W, "graph", False):
+        out["graph_replay"] = {
+            "what": "the same fwd+bwd step captured once with torch.cuda.graph and replayed "
+                    f"{steps} times (the eager step above is bound by host-side launch "
+                    "overhead at this size)",
+            "value": round(job_throughput(units, steps, world, g_ms, scale), 3),
+            "unit": W.unit, "ms_per_step": round(g_ms / steps, 4),
+            "gpu_launches_per_step": int(g_launches)}
     if not full:
         return out
     name, fn, work, bound = W.kernel(st)
@@ -1073,6 +1127,8 @@ def run_ours(args, rank, world, local_rank):
                         "e2e": c.get("e2e")}
                 if "cpu_baseline" in c:
                     line["cpu_baseline"] = c["cpu_baseline"]
+                if "graph_replay" in c:
+                    line["graph_replay"] = c["graph_replay"]
             elif configs:
                 line["configs"] = configs
             print(json.dumps(line), flush=True)
