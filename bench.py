@@ -1106,7 +1106,8 @@ def run_ours(args, rank, world, local_rank):
         fp32_peak = fp32_fma_peak(dev) if names else None
         configs = {}
         for k in names:
-            configs[k] = measure_config(WORKLOADS[k], args, world, dev, barrier, None, fp32_peak)
+            configs[k] = measure_config(WORKLOADS[k], args, world, dev, barrier, None, fp32_peak,
+                                        batch=args.batch)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             torch.cuda.synchronize()
             if line is not None:
@@ -1204,6 +1205,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--rows", type=int, default=None,
                     help="cfg2 only: rows per GPU (default: the config's; fewer for profiling)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="the other configs: batch per GPU (default: the config's; smaller for "
+                         "profiling)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
