@@ -768,6 +768,7 @@ constexpr int kLM[] = {2, 4, 6, 8, 10, 12, 16, 20, 24, 32, 40, 64};
 #include "dwt_syn_tile.cuh"
 #include "dwt_stream.cuh"
 #include "dwt_stream2.cuh"
+#include "dwt_stream3.cuh"
 
 namespace fdwt {
 namespace dwtk {
@@ -977,9 +978,9 @@ int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
         const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
         cudaStream_t stream, size_t* ws_needed, bool allow_stream = true);
 
-// Analysis whose finest levels stream (dwt_stream.cuh, dwt_stream2.cuh): from the finest level
-// on, each pair of levels that fuses runs as one two-level pass, else each level that streams as
-// a one-level pass; the approximations are handed over through two alternating workspace
+// Analysis whose finest levels stream (dwt_stream.cuh, dwt_stream2.cuh, dwt_stream3.cuh): from
+// the finest level on, each triple of levels that fuses runs as one three-level pass, else each
+// pair that fuses as a two-level pass, else each level that streams as a one-level pass; the approximations are handed over through two alternating workspace
 // regions; the remaining (short-row) levels run on the cluster kernel after them.
 // FDWT_ERR_UNSUPPORTED when the finest level does not stream (or x is not 16-byte aligned).
 template <typename T, int LM>
@@ -992,7 +993,12 @@ int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv,
   std::vector<std::pair<int, int>> stages;  // (first level, levels)
   int c = 0;
   while (c < nl) {
-    if (c + 1 < nl && plan_ana2<T, LM>(std::max<int64_t>(rows, 1), lv[c], lv[c + 1], off).ok) {
+    if (c + 2 < nl &&
+        plan_ana3<T, LM>(std::max<int64_t>(rows, 1), lv[c], lv[c + 1], lv[c + 2], off).ok) {
+      stages.emplace_back(c, 3);
+      c += 3;
+    } else if (c + 1 < nl &&
+               plan_ana2<T, LM>(std::max<int64_t>(rows, 1), lv[c], lv[c + 1], off).ok) {
       stages.emplace_back(c, 2);
       c += 2;
     } else if (ana_streams<T, LM>(lv[c])) {
@@ -1031,9 +1037,11 @@ int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv,
   for (int i = 0; i < ns; ++i) {
     const int k = stages[i].first, m = stages[i].second;
     void* a_out = k + m - 1 == nl - 1 ? dst_final : static_cast<void*>(reg[i & 1]);
-    int st = m == 2 ? run_ana2_stream<T, LM>(rows, src, lv[k], lv[k + 1], a_out, h0, h1, L, off,
-                                             stream)
-                    : run_ana_stream<T, LM>(rows, src, lv[k], a_out, h0, h1, L, off, stream);
+    int st = m == 3 ? run_ana3_stream<T, LM>(rows, src, lv[k], lv[k + 1], lv[k + 2], a_out, h0,
+                                             h1, L, off, stream)
+             : m == 2 ? run_ana2_stream<T, LM>(rows, src, lv[k], lv[k + 1], a_out, h0, h1, L, off,
+                                               stream)
+                      : run_ana_stream<T, LM>(rows, src, lv[k], a_out, h0, h1, L, off, stream);
     if (st == FDWT_ERR_UNSUPPORTED && m == 1)  // this level on the cluster kernel
       st = run<T, LM, true>(rows, src, std::vector<Level>(1, lv[k]), a_out, h0, h1, L, off,
                             nullptr, 0, stream, nullptr, false);
