@@ -43,11 +43,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "DWT/CWT achieved HBM GB/s (% of B200 peak); Morlet mixer tokens/s fwd+bwd"
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) per full-size launch of the kernels of the two finest levels, from
-# one ncu capture of each on 1024 of the 2048 rows scaled by 2 (traffic grows with the rows);
-# the captures are summarised in profiles/dwt_cfg2_kernels.txt
+# DRAM bytes (read + write) per full-size launch of the finest analysis and synthesis passes,
+# from one ncu capture of each on 1024 of the 2048 rows scaled by 2 (traffic grows with the
+# rows); the captures are summarised in profiles/dwt_cfg2_kernels.txt
 TRAFFIC_PER_LAUNCH = {
-    "dwt_ana2_stream_kernel<float,16>": 974_800_000,
+    "dwt_ana3_stream_kernel<float,16>": 973_150_000,
     "dwt_syn2_stream_kernel<float,16,0>": 970_000_000,
 }
 CONFIG_NAMES = ["cfg1", "cfg3", "cfg3l", "cfg4", "cfg5", "cfg5c"]
@@ -320,12 +320,13 @@ class Cfg2(Workload):
         return x.grad
 
     def kernels(self, st):
-        """The two finest levels of the step's analysis / synthesis in one launch each."""
+        """The finest pass of the step's analysis (levels 1-3 in one launch) and of its
+        synthesis (levels 2-1 in one launch)."""
         F = st["F"]
         x2 = st["x"].detach().reshape(-1, self.shape[-1])
         c2 = F.wavedec(x2, st["bank"], self.mode, 2)
-        return {"dwt_ana2_stream_kernel<float,16>":
-                lambda: F.wavedec(x2, st["bank"], self.mode, 2),
+        return {"dwt_ana3_stream_kernel<float,16>":
+                lambda: F.wavedec(x2, st["bank"], self.mode, 3),
                 "dwt_syn2_stream_kernel<float,16,0>":
                 lambda: F.waverec(c2, st["bank"], self.mode)}
 
@@ -1022,9 +1023,9 @@ def run_headline(args, rank, world, local_rank, cpu):
             "launch_ms": round(kern_ms, 4),
             "traffic": TRAFFIC_PER_LAUNCH.get(dominant),
             "kernels_ms_per_launch": {k: round(v, 4) for k, v in kern.items()},
-            "launch": "the two finest levels of the step's analysis / synthesis in one launch "
-                      "over every row: x (or the level-1 details and level-2 coefficients) "
-                      "read once, the other side written once",
+            "launch": "the finest pass of the step's analysis (levels 1-3) / synthesis "
+                      "(levels 2-1), one launch over every row: x (or the level-1 details and "
+                      "level-2 coefficients) read once, the other side written once",
             "calls_ms": {"wavedec (8 levels)": round(ana_ms, 4),
                          "waverec (8 levels)": round(syn_ms, 4)},
         },
