@@ -37,34 +37,48 @@ _MAX_OCT, _MAX_SCALES, _MAX_LP = 24, 256, 49
 
 
 def freqs_to_scales(freqs, fs: float = 1.0, w0: float = 6.0) -> torch.Tensor:
-    """Scale (in samples) whose Morlet centre frequency is ``freqs`` (same unit as ``fs``)."""
+    """Morlet scale, in samples, whose centre frequency is ``freqs`` (in the unit of ``fs``):
+    ``w0 fs / (2 pi f)``, as fp64."""
     f = torch.as_tensor(freqs, dtype=torch.float64)
     return w0 * fs / (2 * math.pi * f)
 
 
 def scales_to_freqs(scales, fs: float = 1.0, w0: float = 6.0) -> torch.Tensor:
+    """Inverse of :func:`freqs_to_scales` (the same expression with the roles swapped)."""
     s = torch.as_tensor(scales, dtype=torch.float64)
     return w0 * fs / (2 * math.pi * s)
 
 
 def _halfband(c: int, beta: float) -> torch.Tensor:
-    """Kaiser-windowed half-band low-pass, 2c+1 taps, unit DC gain (``fdwt/cwt.py:65-68``)."""
-    n = torch.arange(-c, c + 1, dtype=torch.float64)
-    h = 0.5 * torch.sinc(n / 2) * torch.from_numpy(np.kaiser(2 * c + 1, beta))
-    return h / h.sum()
-
-
-def _next_pow2(v: int) -> int:
-    return 1 if v <= 1 else 1 << (int(v) - 1).bit_length()
+    """The pyramid's anti-aliasing filter: 2c+1 taps of sinc(t/2) under a Kaiser window,
+    scaled to unit DC gain (the reference designs the same filter, ``fdwt/cwt.py:65-68``)."""
+    t = torch.arange(-c, c + 1, dtype=torch.float64)
+    taps = torch.sinc(t / 2) * torch.from_numpy(np.kaiser(2 * c + 1, beta))
+    return taps / taps.sum()
 
 
 @dataclass
 class _Stage:
+    """The scales that share one octave of the pyramid."""
     octave: int
-    dil: int                # filter dilation 2**octave
-    scale_idx: List[int]    # global scale indices, sorted by support
-    half: int               # filters have 2*half+1 taps (at spacing `dil`)
-    support: List[int]      # per scale half-support (taps)
+    dil: int                # tap spacing 2**octave in samples of x
+    scale_idx: List[int]    # the scales' user indices, in increasing support
+    half: int               # the octave's filters span taps -half .. half
+    support: List[int]      # half-support (in taps) of each scale, same order
+
+
+def _octave_of(scale: float, s_th: float, pyramid: bool) -> int:
+    """Octave that computes ``scale``: the largest j >= 0 with 2^j s_th <= scale (0 unless
+    the transform runs on the pyramid)."""
+    if not pyramid:
+        return 0
+    return max(0, math.floor(math.log2(scale / s_th)))
+
+
+def _support_taps(scale: float, reach: float, dil: int) -> int:
+    """Half-support in taps of spacing ``dil``: the Gaussian envelope is cut at ``reach``
+    scale units (at least one tap)."""
+    return max(1, math.ceil(reach * scale / dil))
 
 
 class _PlanC(ctypes.Structure):
@@ -80,12 +94,18 @@ class _PlanC(ctypes.Structure):
 
 
 class MorletPlan:
-    """Static description of a Morlet CWT: scale grouping, filter sizes and margins.
+    """What a Morlet CWT needs besides the signal: the octave of each scale, the filter
+    supports and the pyramid margins.  It depends on the initial scales only, so learnable
+    scales reuse one plan while :meth:`filters` resamples the current ones.
 
-    Reproduces the reference's ``MorletPlan`` (``fdwt/cwt.py:80-203``) exactly: octave j holds
-    the scales in ``[2^j s_th, 2^(j+1) s_th)`` with ``s_th = (w0 + truncate) / (0.8 pi)``;
-    supports are ``ceil(truncate * support_margin * s / 2^j)``; the half-band filter has 33
-    (or 49 when ``truncate > 4.5``) taps; ``x_j`` is materialised on ``[-m_j, N + m_j)``.
+    The rules are the reference's (``fdwt/cwt.py:80-203``), restated:
+    - ``s_th = (w0 + truncate) / (0.8 pi)``; with ``method="fast"`` octave j takes the scales
+      in ``[2^j s_th, 2^(j+1) s_th)`` (their band stays under 0.8 pi after j half-band steps),
+      otherwise every scale is in octave 0;
+    - a scale's half-support is ``ceil(truncate * support_margin * s / 2^j)`` taps;
+    - the half-band filter has 33 taps (Kaiser beta 8), or 49 (beta 10) when ``truncate > 4.5``;
+    - ``x_j`` (j >= 1) is kept on ``[-m_j, N + m_j)``: ``m_j`` covers octave j's own reach and
+      that of the half-band steps feeding the coarser octaves.
     """
 
     def __init__(self, scales: Sequence[float], w0: float = 6.0, truncate: float = 4.0,
@@ -95,45 +115,48 @@ class MorletPlan:
             raise ValueError(f"unknown method '{method}' (expected 'fast', 'direct' or 'fft')")
         if norm not in ("l1", "l2"):
             raise ValueError("norm must be 'l1' or 'l2'")
-        scales = [float(s) for s in scales]
-        if not scales or min(scales) <= 0:
+        values = [float(v) for v in scales]
+        if len(values) == 0 or min(values) <= 0:
             raise ValueError("scales must be a non-empty sequence of positive numbers")
-        self.scales, self.w0, self.truncate, self.norm = scales, float(w0), float(truncate), norm
+        self.scales = values
+        self.w0, self.truncate, self.norm = float(w0), float(truncate), norm
         self.complex, self.method = bool(complex), method
-        self.channels = 2 if complex else 1
+        self.channels = 2 if self.complex else 1
+        self.s_th = (w0 + truncate) / (0.8 * math.pi)
         reach = truncate * support_margin
 
-        self.s_th = (w0 + truncate) / (0.8 * math.pi)
-        groups: Dict[int, List[int]] = {}
-        for i, s in enumerate(scales):
-            j = 0 if method != "fast" else max(0, math.floor(math.log2(s / self.s_th)))
-            groups.setdefault(j, []).append(i)
+        octave = [_octave_of(v, self.s_th, method == "fast") for v in values]
         self.stages: List[_Stage] = []
-        for j in sorted(groups):
-            dil = 2 ** j
-            sup = {i: max(1, math.ceil(reach * scales[i] / dil)) for i in groups[j]}
-            idx = sorted(groups[j], key=lambda i: sup[i])
-            self.stages.append(_Stage(j, dil, idx, max(sup.values()), [sup[i] for i in idx]))
+        for j in sorted(set(octave)):
+            dil = 1 << j
+            members = [i for i, o in enumerate(octave) if o == j]
+            taps = {i: _support_taps(values[i], reach, dil) for i in members}
+            members.sort(key=taps.__getitem__)  # stable: equal supports keep the user's order
+            supports = [taps[i] for i in members]
+            self.stages.append(_Stage(j, dil, members, max(supports), supports))
         self.n_octaves = self.stages[-1].octave + 1
         self.center = max(st.half for st in self.stages)
-        self._dil = [0.0] * len(scales)
-        self._sup = [0.0] * len(scales)
+        # per user scale: its tap spacing and half-support (the filters' sampling grid)
+        self._dil = [0.0] * len(values)
+        self._sup = [0.0] * len(values)
         for st in self.stages:
             for i, c in zip(st.scale_idx, st.support):
-                self._dil[i], self._sup[i] = float(st.dil), float(c)
+                self._dil[i] = float(st.dil)
+                self._sup[i] = float(c)
 
+        pyramid = self.n_octaves > 1
         c_lp, beta = (16, 8.0) if truncate <= 4.5 else (24, 10.0)
-        multi = self.n_octaves > 1
-        self.lowpass = _halfband(c_lp, beta) if multi else torch.zeros(1, dtype=torch.float64)
-        self.c_lp = c_lp if multi else 0
+        self.c_lp = c_lp if pyramid else 0
+        self.lowpass = _halfband(c_lp, beta) if pyramid else torch.zeros(1, dtype=torch.float64)
 
-        J = self.n_octaves - 1
-        by_oct = {st.octave: st for st in self.stages}
-        self.margins = [0] * (J + 1)
-        for j in range(J, 0, -1):
-            own = by_oct[j].half * 2 ** j if j in by_oct else 0
-            nxt = self.margins[j + 1] + self.c_lp * 2 ** j if j < J else 0
-            self.margins[j] = max(own, nxt)
+        # margins, coarse to fine: octave j's own filter reach, or what the half-band step
+        # into x_{j+1} needs to leave x_{j+1}'s margin exact, whichever is larger
+        last = self.n_octaves - 1
+        reach_of = {st.octave: st.half * st.dil for st in self.stages}
+        self.margins = [0] * (last + 1)
+        for j in range(last, 0, -1):
+            feed = self.margins[j + 1] + self.c_lp * (1 << j) if j < last else 0
+            self.margins[j] = max(reach_of.get(j, 0), feed)
         self._static_cache: Dict = {}
         self._capi_struct = None
 
@@ -142,35 +165,39 @@ class MorletPlan:
         return len(self.scales)
 
     def halfband_taps(self, device, dtype) -> torch.Tensor:
-        """``taps[t] = lowpass[c_lp + t]`` (t = 0..c_lp), as the reference exposes it."""
+        """The half-band taps from the centre out, ``lowpass[c_lp + t]`` for t = 0..c_lp (the
+        reference exposes the same accessor)."""
         key = ("hb", torch.device(device), dtype)
         if key not in self._static_cache:
             self._static_cache[key] = self.lowpass[self.c_lp:].to(device=device, dtype=dtype)
         return self._static_cache[key]
 
     def filters(self, scales: torch.Tensor, w0, dtype: torch.dtype) -> torch.Tensor:
-        """All sampled Morlet filters as one ``(S*C, 2*center+1)`` tensor (row ``i*C + c``).
+        """Every sampled filter in one ``(S*C, 2*center+1)`` tensor, row ``i*C + c`` (c = 0 the
+        real part, 1 the imaginary part), centre tap at column ``center``.
 
-        Scale ``i`` is sampled with the spacing (dilation) of its octave and truncated to its
-        support.  Differentiable w.r.t. ``scales`` and ``w0`` (when it is a tensor).  Same
-        expression as the reference (``fdwt/cwt.py:181-203``).
+        Scale i is sampled at its octave's tap spacing d: tap k sits at ``u = k d / s`` scale
+        units, and its value is ``pi^(-1/4) (d / n(s)) (e^{i w0 u} - e^{-w0^2/2}) e^{-u^2/2}``
+        inside the scale's support and 0 outside, n(s) = sqrt(s) for the l2 norm, s for l1 (the
+        factor d makes the dilated sum a Riemann sum of spacing d).  Differentiable in
+        ``scales`` and in ``w0`` when it is a tensor; computed in fp64.
         """
-        dev = scales.device
         f64 = torch.float64
-        s = scales.to(f64)[:, None]
-        dil = torch.tensor(self._dil, dtype=f64, device=dev)[:, None]
-        sup = torch.tensor(self._sup, dtype=f64, device=dev)[:, None]
-        k = torch.arange(-self.center, self.center + 1, device=dev, dtype=f64)[None, :]
-        t = k * dil / s
-        env = torch.exp(-0.5 * t * t) * (k.abs() <= sup)
-        amp = _PI_M14 * dil / (s.sqrt() if self.norm == "l2" else s)
-        w0_ = torch.as_tensor(w0, dtype=f64, device=dev)
-        w0t = w0_ * t
-        re = (torch.cos(w0t) - torch.exp(-0.5 * w0_ * w0_)) * env * amp
+        dev = scales.device
+        s = scales.to(f64).unsqueeze(1)
+        spacing = torch.tensor(self._dil, dtype=f64, device=dev).unsqueeze(1)
+        limit = torch.tensor(self._sup, dtype=f64, device=dev).unsqueeze(1)
+        k = torch.arange(-self.center, self.center + 1, dtype=f64, device=dev).unsqueeze(0)
+        u = k * spacing / s
+        window = torch.exp(-0.5 * u * u) * (k.abs() <= limit)
+        gain = _PI_M14 * spacing / (s.sqrt() if self.norm == "l2" else s)
+        wave = torch.as_tensor(w0, dtype=f64, device=dev)
+        phase = wave * u
+        real = (torch.cos(phase) - torch.exp(-0.5 * wave * wave)) * window * gain
         if not self.complex:
-            return re.to(dtype)
-        im = torch.sin(w0t) * env * amp
-        return torch.stack([re, im], 1).reshape(-1, k.shape[1]).to(dtype)
+            return real.to(dtype)
+        imag = torch.sin(phase) * window * gain
+        return torch.stack((real, imag), dim=1).reshape(-1, k.shape[1]).to(dtype)
 
     def capi(self) -> _PlanC:
         """The plan as the C struct the kernels take (built once)."""
@@ -350,39 +377,53 @@ def _apply_plan(x: torch.Tensor, plan: MorletPlan, H: torch.Tensor) -> torch.Ten
 
 @lru_cache(maxsize=64)
 def _cached_plan(scales: Tuple[float, ...], w0, truncate, norm, complex, method) -> MorletPlan:
+    """Plans of the functional :func:`cwt`, shared between calls with the same arguments."""
     return MorletPlan(scales, w0, truncate, norm, complex, method)
 
 
 @lru_cache(maxsize=64)
 def _cached_filters(plan: MorletPlan, device: torch.device, dtype: torch.dtype):
-    s = torch.tensor(plan.scales, dtype=torch.float64, device=device)
-    return plan.filters(s, plan.w0, dtype)
+    """The fixed filters of a cached plan on one device, in one dtype."""
+    return plan.filters(torch.tensor(plan.scales, dtype=torch.float64, device=device), plan.w0,
+                        dtype)
 
 
 def _resolve_scales(scales, freqs, fs, w0) -> List[float]:
+    """The scales in samples from exactly one of ``scales`` / ``freqs`` (with ``fs``, ``w0``)."""
     if (scales is None) == (freqs is None):
         raise ValueError("pass exactly one of `scales` or `freqs`")
-    s = freqs_to_scales(freqs, fs, w0) if freqs is not None else torch.as_tensor(
-        scales, dtype=torch.float64)
-    return [float(v) for v in s.flatten()]
+    if freqs is not None:
+        values = freqs_to_scales(freqs, fs, w0)
+    else:
+        values = torch.as_tensor(scales, dtype=torch.float64)
+    return values.flatten().tolist()
+
+
+def _compute_dtype(x: torch.Tensor) -> torch.dtype:
+    return torch.float64 if x.dtype == torch.float64 else torch.float32
 
 
 def cwt(x: torch.Tensor, scales: Optional[Sequence[float]] = None, *, freqs=None, fs: float = 1.0,
         w0: float = 6.0, method: str = "fast", norm: str = "l2", complex: bool = True,
         truncate: float = 4.0) -> torch.Tensor:
-    """Morlet CWT along the last dimension: ``(..., N)`` -> ``(..., S, N)`` complex."""
-    s = _resolve_scales(scales, freqs, fs, w0)
-    plan = _cached_plan(tuple(s), float(w0), float(truncate), norm, bool(complex), method)
-    dt = torch.float64 if x.dtype == torch.float64 else torch.float32
-    return _apply_plan(x, plan, _cached_filters(plan, x.device, dt))
+    """Morlet CWT of the real rows ``x (..., N)``: ``(..., S, N)``, complex unless
+    ``complex=False``.  Give the scales in samples (``scales``) or as centre frequencies in
+    the unit of ``fs`` (``freqs``, ``scale = w0 fs / (2 pi f)``); ``method`` is ``"fast"``
+    (octave pyramid), ``"direct"`` (every scale at full rate) or ``"fft"``."""
+    plan = _cached_plan(tuple(_resolve_scales(scales, freqs, fs, w0)), float(w0),
+                        float(truncate), norm, bool(complex), method)
+    return _apply_plan(x, plan, _cached_filters(plan, x.device, _compute_dtype(x)))
 
 
 class CWT1D(nn.Module):
-    """Morlet continuous wavelet transform as a module (``fdwt/cwt.py:654-716``).
+    """The Morlet CWT as a module (the reference's ``CWT1D``, ``fdwt/cwt.py:654-716``): real
+    ``(..., N)`` in, ``(..., S, N)`` complex out (real with ``complex=False``).
 
-    Input ``(..., N)`` real, output ``(..., S, N)`` complex (or real with ``complex=False``).
-    With ``learnable=True`` the (log-)scales are parameters; ``learnable_w0`` also learns the
-    Morlet wave number.
+    ``learnable=True`` makes the log-scales a parameter (``log_scales``, fp32) and
+    ``learnable_w0=True`` the wave number (``w0``); gradients reach them through the
+    filter-gradient kernels.  Otherwise ``log_scales`` is a buffer, ``w0`` a float, and the
+    sampled filters are cached per device and dtype.  ``support_margin`` (default 1.25 when
+    learning, else 1) widens the filter supports so that scales can grow.
     """
 
     def __init__(self, freqs=None, scales=None, fs: float = 1.0, w0: float = 6.0,
@@ -390,51 +431,51 @@ class CWT1D(nn.Module):
                  truncate: float = 4.0, learnable: bool = False, learnable_w0: bool = False,
                  support_margin: Optional[float] = None):
         super().__init__()
-        s = _resolve_scales(scales, freqs, fs, w0)
-        if support_margin is None:
-            support_margin = 1.25 if learnable else 1.0
+        values = _resolve_scales(scales, freqs, fs, w0)
+        margin = support_margin if support_margin is not None else (1.25 if learnable else 1.0)
         self.fs = fs
-        self.plan = MorletPlan(s, w0, truncate, norm, complex, method, support_margin)
-        log_s = torch.tensor(s, dtype=torch.float64).log().float()
+        self.plan = MorletPlan(values, w0, truncate, norm, complex, method, margin)
+        log_scales = torch.tensor(values, dtype=torch.float64).log().float()
         if learnable:
-            self.log_scales = nn.Parameter(log_s)
+            self.log_scales = nn.Parameter(log_scales)
         else:
-            self.register_buffer("log_scales", log_s)
-        if learnable_w0:
-            self.w0 = nn.Parameter(torch.tensor(float(w0)))
-        else:
-            self.w0 = float(w0)
-        self._learn = learnable or learnable_w0
+            self.register_buffer("log_scales", log_scales)
+        self.w0 = nn.Parameter(torch.tensor(float(w0))) if learnable_w0 else float(w0)
+        self._learn = bool(learnable or learnable_w0)
         self._filter_cache: Dict = {}
 
     @property
     def scales(self) -> torch.Tensor:
-        return self.log_scales.exp()
+        """Current scales in samples."""
+        return torch.exp(self.log_scales)
 
     @property
     def w0_value(self) -> float:
-        return float(self.w0.detach()) if isinstance(self.w0, torch.Tensor) else float(self.w0)
+        w = self.w0
+        return float(w.detach()) if isinstance(w, torch.Tensor) else float(w)
 
     @property
     def freqs(self) -> torch.Tensor:
+        """Current centre frequencies in the unit of ``fs``."""
         return scales_to_freqs(self.scales.detach(), self.fs, self.w0_value)
 
     def _filters(self, device, dtype):
-        if self._learn:
-            return self.plan.filters(self.log_scales.to(torch.float64).exp(), self.w0, dtype)
+        if self._learn:  # rebuilt every call: the graph runs back to log_scales / w0
+            return self.plan.filters(torch.exp(self.log_scales.to(torch.float64)), self.w0,
+                                     dtype)
         key = (device, dtype)
-        if key not in self._filter_cache:
-            self._filter_cache = {key: self.plan.filters(self.scales.to(torch.float64), self.w0,
-                                                         dtype)}
-        return self._filter_cache[key]
+        cached = self._filter_cache.get(key)
+        if cached is None:
+            cached = self.plan.filters(self.scales.to(torch.float64), self.w0, dtype)
+            self._filter_cache = {key: cached}
+        return cached
 
     def _apply(self, fn, *args, **kwargs):
-        self._filter_cache = {}
+        self._filter_cache = {}  # moved or cast: the cached filters are stale
         return super()._apply(fn, *args, **kwargs)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        dt = torch.float64 if x.dtype == torch.float64 else torch.float32
-        return _apply_plan(x, self.plan, self._filters(x.device, dt))
+        return _apply_plan(x, self.plan, self._filters(x.device, _compute_dtype(x)))
 
     def extra_repr(self) -> str:
         p = self.plan

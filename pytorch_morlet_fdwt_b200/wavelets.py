@@ -53,30 +53,29 @@ WaveletLike = Union[str, FilterBank, Sequence[Sequence[float]], "pywt.Wavelet"] 
 _CONTINUOUS = ("morl", "morlet", "cmor", "mexh", "gaus1", "shan", "fbsp")
 
 
-def _padded(f: Sequence[float], length: int) -> tuple:
-    vals = tuple(float(v) for v in f)
-    return vals + (0.0,) * (length - len(vals))
+def _as_floats(f: Sequence[float]) -> tuple:
+    return tuple(float(v) for v in f)
 
 
 def get_filter_bank(wavelet: WaveletLike) -> FilterBank:
-    """Resolve ``wavelet`` into a :class:`FilterBank` (``wavelets.py:44-64``).
-
-    Filters are zero padded at the end to a common even length, which leaves the
-    transform unchanged.
+    """A :class:`FilterBank` from a name (``"haar"``, ``"db4"``, ..., any PyWavelets name when
+    PyWavelets is installed), a ``pywt.Wavelet``-like object (``.filter_bank``, ``.name``), a
+    :class:`FilterBank`, or four sequences ``(dec_lo, dec_hi, rec_lo, rec_hi)``
+    (``wavelets.py:44-64``).  The four filters are zero-padded at the end to the longest one's
+    length, rounded up to even; trailing zeros leave the transform unchanged.
     """
     if isinstance(wavelet, FilterBank):
         return wavelet
     if isinstance(wavelet, str):
         return _named_bank(wavelet)
-    if hasattr(wavelet, "filter_bank"):
-        name, bank = getattr(wavelet, "name", "custom"), wavelet.filter_bank
-    else:
-        name, bank = "custom", wavelet
-    if len(bank) != 4:
+    source = getattr(wavelet, "filter_bank", None)
+    name = getattr(wavelet, "name", "custom") if source is not None else "custom"
+    filters = source if source is not None else wavelet
+    if len(filters) != 4:
         raise ValueError("a custom filter bank must be (dec_lo, dec_hi, rec_lo, rec_hi)")
-    length = max(len(f) for f in bank)
-    length += length % 2
-    return FilterBank(name, *(_padded(f, length) for f in bank))
+    filters = [_as_floats(f) for f in filters]
+    even = -(-max(len(f) for f in filters) // 2) * 2
+    return FilterBank(name, *(f + (0.0,) * (even - len(f)) for f in filters))
 
 
 def daubechies_scaling_filter(order: int) -> np.ndarray:
@@ -134,10 +133,8 @@ def _named_bank(name: str) -> FilterBank:
 
 @lru_cache(maxsize=None)
 def _as_tensors(bank: FilterBank, device: torch.device, dtype: torch.dtype) -> dict:
-    mk = lambda f: torch.tensor(f, dtype=dtype, device=device)  # noqa: E731
-    return {
-        "dec_lo": mk(bank.dec_lo),
-        "dec_hi": mk(bank.dec_hi),
-        "rec_lo_rev": mk(bank.rec_lo[::-1]),
-        "rec_hi_rev": mk(bank.rec_hi[::-1]),
-    }
+    """The analysis filters as they are, the synthesis filters time-reversed (the reference's
+    synthesis is the transpose of an analysis by the reversed filters)."""
+    taps = {"dec_lo": bank.dec_lo, "dec_hi": bank.dec_hi,
+            "rec_lo_rev": bank.rec_lo[::-1], "rec_hi_rev": bank.rec_hi[::-1]}
+    return {k: torch.tensor(v, dtype=dtype, device=device) for k, v in taps.items()}
