@@ -16,7 +16,9 @@ optional NCCL all-gather of the per-rank results, timed apart).
 
 The same line carries ``configs``: every other baseline config (cfg1, cfg3, cfg3 learnable,
 cfg4, cfg5 and its channel-mix variant), each measured the same way with its own roofline
-(HBM bytes, or FP32 FMA work for the fused mixers), ``e2e`` and CPU baseline.
+(HBM bytes, or FP32 FMA work for the fused mixers), ``e2e`` and CPU baseline, and
+``mode_sweep``: the headline shape's wavedec and waverec calls in each of the five boundary
+modes.
 
 CPU baseline and the reference arm (``--impl reference``): the reference package's own CPU
 PyTorch path (``fdwt`` installed under ``baseline/_ref``, called with CPU tensors, all host
@@ -1038,6 +1040,46 @@ def run_headline(args, rank, world, local_rank, cpu):
     return line
 
 
+def run_mode_sweep(args, world, dev, barrier):
+    """The headline shape in each of the five boundary modes: one wavedec and one waverec call
+    per mode (forward only: the backward of each call runs the other's kernels), device-timed
+    over back-to-back calls, max over ranks.  Bytes per call are the algorithmic ones of that
+    mode (x once, every coefficient array once)."""
+    import torch
+    import pytorch_morlet_fdwt_b200 as F
+    W = WORKLOADS["cfg2"]
+    bank = F.get_filter_bank(W.wavelet)
+    torch.manual_seed(4321 + (dev.index or 0))
+    x = torch.randn((W.batch,) + W.shape, device=dev)
+    rows = x.numel() // W.shape[-1]
+    peak, _ = peaks()
+    reps = max(3, args.steps)
+    out = {}
+    with torch.no_grad():
+        for mode in ("periodization", "zero", "periodic", "symmetric", "reflect"):
+            lens = _dwt_lens(W.shape[-1], 16, mode, W.level)
+            nbytes = (W.shape[-1] + sum(lens) + lens[-1]) * 4 * rows
+            c = F.wavedec(x, bank, mode, W.level)
+            a_ms, a_l = time_call(lambda: F.wavedec(x, bank, mode, W.level), reps, barrier)
+            s_ms, s_l = time_call(lambda: F.waverec(c, bank, mode), reps, barrier)
+            a_ms, s_ms = max_over_ranks([a_ms, s_ms], world, dev)
+            a_gbs = nbytes * world / (a_ms / 1e3) / 1e9
+            s_gbs = nbytes * world / (s_ms / 1e3) / 1e9
+            out[mode] = {"bytes_per_call_per_gpu": nbytes,
+                         "wavedec_ms": round(a_ms, 4), "wavedec_gbs": round(a_gbs, 1),
+                         "wavedec_frac": round(a_gbs / world / peak, 4),
+                         "wavedec_launches": a_l,
+                         "waverec_ms": round(s_ms, 4), "waverec_gbs": round(s_gbs, 1),
+                         "waverec_frac": round(s_gbs / world / peak, 4),
+                         "waverec_launches": s_l}
+            del c
+    del x
+    torch.cuda.empty_cache()
+    return {"what": "db8 level-8 wavedec / waverec of x float32 (16, 128, 65536) per GPU in "
+                    "every boundary mode; GB/s over all GPUs, frac of the measured HBM copy "
+                    "bandwidth per GPU", "modes": out}
+
+
 def run_strong_and_gather(args, rank, world, local_rank):
     """At N > 1: the headline config with its batch split over the ranks (strong scaling), and
     the optional NCCL all-gather of the per-rank input gradients, timed apart."""
@@ -1100,6 +1142,10 @@ def run_ours(args, rank, world, local_rank):
     barrier = dist.barrier if world > 1 else (lambda: None)
     try:
         line = run_headline(args, rank, world, local_rank, None) if headline else None
+        if headline and args.rows is None and not args.no_modes:
+            sweep = run_mode_sweep(args, world, dev, barrier)
+            if line is not None:
+                line["mode_sweep"] = sweep
         if world > 1 and headline and args.rows is None:
             extra = run_strong_and_gather(args, rank, world, local_rank)
             if line is not None:
@@ -1204,6 +1250,8 @@ def main():
                          "'configs'), or one config alone")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-modes", action="store_true",
+                    help="skip the five-mode sweep of the headline shape")
     ap.add_argument("--rows", type=int, default=None,
                     help="cfg2 only: rows per GPU (default: the config's; fewer for profiling)")
     ap.add_argument("--batch", type=int, default=None,
