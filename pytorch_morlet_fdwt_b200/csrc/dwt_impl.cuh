@@ -980,28 +980,36 @@ int run(int64_t rows, const void* src0, std::vector<Level> lv, void* dst_final,
 
 // Analysis whose finest levels stream (dwt_stream.cuh, dwt_stream2.cuh, dwt_stream3.cuh): from
 // the finest level on, each triple of levels that fuses runs as one three-level pass, else each
-// pair that fuses as a two-level pass, else each level that streams as a one-level pass; the approximations are handed over through two alternating workspace
-// regions; the remaining (short-row) levels run on the cluster kernel after them.
+// pair that fuses as a two-level pass, else each level that streams as a one-level pass; the
+// approximations are handed over through two alternating workspace regions; the remaining
+// (short-row) levels run on the cluster kernel after them.  A handover between two streaming
+// stages stores its rows 16 bytes apart (length rounded up), so that the next stage's bulk
+// copies start on 16-byte boundaries whatever the coefficient lengths (odd in every mode but
+// periodization); the handover into the cluster kernel stays unpadded.
 // FDWT_ERR_UNSUPPORTED when the finest level does not stream (or x is not 16-byte aligned).
 template <typename T, int LM>
 int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv, void* dst_final,
                    const double* h0, const double* h1, int L, int off, void* ws, size_t ws_bytes,
                    cudaStream_t stream, size_t* ws_needed) {
+  using A = typename AccOf<T>::type;
+  constexpr int64_t VW = 16 / static_cast<int64_t>(sizeof(A));
   const int nl = static_cast<int>(lv.size());
   if (ws_needed == nullptr && (reinterpret_cast<uintptr_t>(src0) & 15) != 0)
     return FDWT_ERR_UNSUPPORTED;
+  // input row stride of level c when a streaming stage feeds it (x itself for c = 0)
+  auto pitch = [&](int c) { return c == 0 ? lv[0].n_in : (lv[c].n_in + VW - 1) / VW * VW; };
+  const int64_t r1 = std::max<int64_t>(rows, 1);
   std::vector<std::pair<int, int>> stages;  // (first level, levels)
   int c = 0;
   while (c < nl) {
-    if (c + 2 < nl &&
-        plan_ana3<T, LM>(std::max<int64_t>(rows, 1), lv[c], lv[c + 1], lv[c + 2], off).ok) {
+    const int64_t xs = pitch(c);
+    if (c + 2 < nl && plan_ana3<T, LM>(r1, lv[c], lv[c + 1], lv[c + 2], off, xs).ok) {
       stages.emplace_back(c, 3);
       c += 3;
-    } else if (c + 1 < nl &&
-               plan_ana2<T, LM>(std::max<int64_t>(rows, 1), lv[c], lv[c + 1], off).ok) {
+    } else if (c + 1 < nl && plan_ana2<T, LM>(r1, lv[c], lv[c + 1], off, xs).ok) {
       stages.emplace_back(c, 2);
       c += 2;
-    } else if (ana_streams<T, LM>(lv[c])) {
+    } else if (ana_streams<T, LM>(lv[c], xs)) {
       stages.emplace_back(c, 1);
       c += 1;
     } else {
@@ -1010,11 +1018,16 @@ int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv,
   }
   if (stages.empty()) return FDWT_ERR_UNSUPPORTED;
   const int ns = static_cast<int>(stages.size());
+  // approximation row stride of stage i: padded when the next stage streams
+  auto out_pitch = [&](int i) {
+    const int last = stages[i].first + stages[i].second - 1;
+    return i + 1 < ns ? pitch(last + 1) : lv[last].a_len;
+  };
   size_t region[2] = {0, 0};
   for (int i = 0; i < ns; ++i) {
     const int last = stages[i].first + stages[i].second - 1;
     if (last == nl - 1) continue;
-    const size_t b = (static_cast<size_t>(rows) * lv[last].a_len * sizeof(T) + 255) & ~size_t(255);
+    const size_t b = (static_cast<size_t>(rows) * out_pitch(i) * sizeof(T) + 255) & ~size_t(255);
     region[i & 1] = std::max(region[i & 1], b);
   }
   const std::vector<Level> rest(lv.begin() + c, lv.end());
@@ -1037,12 +1050,16 @@ int run_ana_stages(int64_t rows, const void* src0, const std::vector<Level>& lv,
   for (int i = 0; i < ns; ++i) {
     const int k = stages[i].first, m = stages[i].second;
     void* a_out = k + m - 1 == nl - 1 ? dst_final : static_cast<void*>(reg[i & 1]);
-    int st = m == 3 ? run_ana3_stream<T, LM>(rows, src, lv[k], lv[k + 1], lv[k + 2], a_out, h0,
-                                             h1, L, off, stream)
-             : m == 2 ? run_ana2_stream<T, LM>(rows, src, lv[k], lv[k + 1], a_out, h0, h1, L, off,
-                                               stream)
-                      : run_ana_stream<T, LM>(rows, src, lv[k], a_out, h0, h1, L, off, stream);
-    if (st == FDWT_ERR_UNSUPPORTED && m == 1)  // this level on the cluster kernel
+    const int64_t xs = pitch(k), as = out_pitch(i);
+    int st = m == 3 ? run_ana3_stream<T, LM>(rows, src, lv[k], lv[k + 1], lv[k + 2], xs, a_out,
+                                             as, h0, h1, L, off, stream)
+             : m == 2 ? run_ana2_stream<T, LM>(rows, src, lv[k], lv[k + 1], xs, a_out, as, h0,
+                                               h1, L, off, stream)
+                      : run_ana_stream<T, LM>(rows, src, lv[k], xs, a_out, as, h0, h1, L, off,
+                                              stream);
+    // a one-level stage with unpadded rows on both sides can run on the cluster kernel; any
+    // other refusal sends the whole call to the cluster plan
+    if (st == FDWT_ERR_UNSUPPORTED && m == 1 && xs == lv[k].n_in && as == lv[k].a_len)
       st = run<T, LM, true>(rows, src, std::vector<Level>(1, lv[k]), a_out, h0, h1, L, off,
                             nullptr, 0, stream, nullptr, false);
     if (st != FDWT_OK) return st;

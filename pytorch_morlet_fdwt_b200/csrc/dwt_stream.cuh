@@ -406,8 +406,8 @@ constexpr int ana_stream_tile() { return 2 * SNT * ana_stream_v<A>(); }
 
 template <typename A, int LM>
 struct AnaStreamParams {
-  const A* x;        // (rows, n)
-  A* ap;             // (rows, a_len) approximation (a_len = nc or nc + 1: trailing zero)
+  const A* x;        // (rows, xs) input
+  A* ap;             // (rows, as) approximation (a_len = nc or nc + 1: trailing zero)
   A* dp;             // (rows, nc) details
   int* err;          // device error word
   uint32_t dbg_tx;   // test hook: extra expected bytes of global tile 0's copy
@@ -415,6 +415,8 @@ struct AnaStreamParams {
   int64_t ntile;     // rows * tiles
   int64_t P;         // period of the boundary mode
   int32_t n, nc, a_len, off, mode, tiles, span;
+  int32_t xs, as;    // row strides of x and of the approximation (xs a multiple of 16 bytes)
+  int32_t n_al;      // n rounded down to 16 bytes: the bulk copies end there
   int32_t T;         // outputs per tile (a multiple of 2 V)
   alignas(16) A taps[2 * LM];  // (h0[j], h1[j]) interleaved
 };
@@ -497,7 +499,7 @@ __device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint6
   auto ext_fill = [&](int64_t g, int s) {
     const int64_t row = g / p.tiles;
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
-    const A* xr = p.x + row * n;
+    const A* xr = p.x + row * p.xs;
     A* sl = slot(s);
     const int l1 = min(xlo + span, 0), r1 = min(xlo + span, pmax + 1);
     auto one = [&](int q) {
@@ -506,17 +508,17 @@ __device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint6
       else cp_async(sl + (q - xlo), xr + e, sizeof(A));
     };
     for (int q = max(xlo, pmin) + tid; q < l1; q += SNT) one(q);
-    for (int q = max(xlo, n) + tid; q < r1; q += SNT) one(q);
+    for (int q = max(xlo, p.n_al) + tid; q < r1; q += SNT) one(q);
     cp_async_commit();
   };
   // one thread: the bulk copy of tile g's in-range input into slot s
   auto issue = [&](int64_t g, int s) {
     const int64_t row = g / p.tiles;
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
-    const int lo = max(xlo, 0), hi = min(xlo + span, n);
+    const int lo = max(xlo, 0), hi = min(xlo + span, p.n_al);
     const unsigned bytes = static_cast<unsigned>(max(hi - lo, 0)) * sizeof(A);
     mbar_expect_tx(&bar[s], bytes + (g == 0 ? p.dbg_tx : 0u));
-    if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * n + lo, bytes, &bar[s]);
+    if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * p.xs + lo, bytes, &bar[s]);
   };
   // the gathers of tile k form the k-th commit group of every thread; the group of tile k + 1
   // is waited for before the barrier that ends tile k
@@ -544,7 +546,7 @@ __device__ void ana_stream_tiles(const AnaStreamParams<A, LM>& p, A* ring, uint6
     if (ok) {
       const int64_t row = g / p.tiles;
       const int t = static_cast<int>(g % p.tiles);
-      A* arow = p.ap + row * p.a_len;
+      A* arow = p.ap + row * p.as;
       A* drow = p.dp + row * p.nc;
       const A* sl = slot(s);
 #pragma unroll 1
@@ -613,28 +615,30 @@ dwt_ana_stream_kernel(const __grid_constant__ AnaStreamParams<A, LM> p, int r) {
 }
 
 // The analysis of level L0 as the streaming kernel when the shape allows it: element type with
-// fp32 / fp64 accumulation, LM <= kStreamMaxLM, rows of a multiple of 16 bytes and at least
-// kStreamMinOut samples.  Shape-only test (pointers are checked at launch).
+// fp32 / fp64 accumulation, LM <= kStreamMaxLM, input rows at least kStreamMinOut samples long
+// and xs apart, xs a multiple of 16 bytes.  Shape-only test (pointers are checked at launch).
 template <typename T, int LM>
-bool ana_streams(const Level& L0) {
+bool ana_streams(const Level& L0, int64_t xs) {
   using A = typename AccOf<T>::type;
   constexpr int VW = 16 / static_cast<int>(sizeof(A));
   return std::is_same<T, A>::value && LM <= kStreamMaxLM && L0.n_in >= kStreamMinOut &&
-         L0.n_in % VW == 0 && L0.n_in <= 0x3fffffffLL && L0.a_len <= L0.n_coef + 1;
+         xs % VW == 0 && xs >= L0.n_in && xs <= 0x3fffffffLL && L0.a_len <= L0.n_coef + 1;
 }
 
-// Runs the one-level analysis of L0 (x: rows x L0.n_in; approximation to a_out, rows x a_len;
-// details to L0.detail) on the streaming kernel; FDWT_ERR_UNSUPPORTED when it does not apply.
+// Runs the one-level analysis of L0 (x: rows of L0.n_in samples, xs apart; approximation to
+// a_out, rows of a_len, as apart; details to L0.detail) on the streaming kernel;
+// FDWT_ERR_UNSUPPORTED when it does not apply.
 template <typename T, int LM>
-int run_ana_stream(int64_t rows, const void* x, const Level& L0, void* a_out, const double* h0,
-                   const double* h1, int L, int off, cudaStream_t stream) {
+int run_ana_stream(int64_t rows, const void* x, const Level& L0, int64_t xs, void* a_out,
+                   int64_t as, const double* h0, const double* h1, int L, int off,
+                   cudaStream_t stream) {
   using A = typename AccOf<T>::type;
   if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
     return FDWT_ERR_UNSUPPORTED;
   } else {
     constexpr int VW = 16 / static_cast<int>(sizeof(A));
     constexpr int V = ana_stream_v<A>();
-    if (!ana_streams<T, LM>(L0) || x == nullptr || a_out == nullptr || L0.detail == nullptr ||
+    if (!ana_streams<T, LM>(L0, xs) || as < L0.a_len || as > 0x3fffffffLL || x == nullptr || a_out == nullptr || L0.detail == nullptr ||
         rows <= 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
       return FDWT_ERR_UNSUPPORTED;
     const int64_t nc = L0.n_coef;
@@ -664,6 +668,9 @@ int run_ana_stream(int64_t rows, const void* x, const Level& L0, void* a_out, co
     p.n = static_cast<int>(L0.n_in);
     p.nc = static_cast<int>(nc);
     p.a_len = static_cast<int>(L0.a_len);
+    p.xs = static_cast<int>(xs);
+    p.as = static_cast<int>(as);
+    p.n_al = static_cast<int>(L0.n_in / VW * VW);
     p.off = off;
     p.mode = L0.mode;
     p.tiles = static_cast<int>(tiles);

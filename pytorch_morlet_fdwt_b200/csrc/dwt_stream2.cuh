@@ -34,9 +34,9 @@ constexpr int ana2_stages() { return sizeof(A) == 8 ? 2 : 3; }
 
 template <typename A, int LM>
 struct Ana2Params {
-  const A* x;        // (rows, n)
+  const A* x;        // (rows, xs)
   A* d1;             // (rows, nc1) level-k details
-  A* a2;             // (rows, a_len2) level-(k+1) approximation
+  A* a2;             // (rows, as) level-(k+1) approximation
   A* d2;             // (rows, nc2) level-(k+1) details
   int* err;          // device error word
   uint32_t dbg_tx;   // test hook: extra expected bytes of global tile 0's copy
@@ -45,6 +45,8 @@ struct Ana2Params {
   int64_t P;         // period of level k's boundary mode on n
   int64_t P2;        // period of level k+1's boundary mode on n1
   int32_t n, nc1, n1, nc2, a_len2, off, mode, mode2, tiles;
+  int32_t xs, as;    // row strides of x and of cA2 (xs a multiple of 16 bytes)
+  int32_t n_al;      // n rounded down to 16 bytes: the bulk copies end there
   int32_t span;      // x elements per ring slot
   int32_t T2;        // level-(k+1) outputs per tile (V q, with K1 = kh + 2q + kr <= 2 SNT)
   int32_t K1, kh;    // level-k items per tile, of which kh before the first owned detail
@@ -70,7 +72,7 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
   auto ext_fill = [&](int64_t g, int s) {
     const int64_t row = g / p.tiles;
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
-    const A* xr = p.x + row * n;
+    const A* xr = p.x + row * p.xs;
     A* sl = slot(s);
     auto one = [&](int q) {
       const int64_t e = ext_index(q, n, p.mode, p.P);
@@ -79,16 +81,16 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
     };
     const int l1 = min(xlo + span, 0), r1 = min(xlo + span, p.x_hi);
     for (int q = xlo + tid; q < l1; q += SNT) one(q);
-    for (int q = max(xlo, n) + tid; q < r1; q += SNT) one(q);
+    for (int q = max(xlo, p.n_al) + tid; q < r1; q += SNT) one(q);
     cp_async_commit();
   };
   auto issue = [&](int64_t g, int s) {
     const int64_t row = g / p.tiles;
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
-    const int lo = max(xlo, 0), hi = min(xlo + span, n);
+    const int lo = max(xlo, 0), hi = min(xlo + span, p.n_al);
     const unsigned bytes = static_cast<unsigned>(max(hi - lo, 0)) * sizeof(A);
     mbar_expect_tx(&bar[s], bytes + (g == 0 ? p.dbg_tx : 0u));
-    if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * n + lo, bytes, &bar[s]);
+    if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * p.xs + lo, bytes, &bar[s]);
   };
 #pragma unroll 1
   for (int s = 0; s < ana2_stages<A>(); ++s) {
@@ -147,7 +149,7 @@ __device__ void ana2_tiles(const Ana2Params<A, LM>& p, A* ring, A* abuf, uint64_
       __syncthreads();
     }
     if (ok) {  // level k+1 from the buffer
-      A* a2row = p.a2 + row * p.a_len2;
+      A* a2row = p.a2 + row * p.as;
       A* d2row = p.d2 + row * p.nc2;
 #pragma unroll 1
       for (int m = tid; m < T2 / V; m += SNT) {
@@ -228,7 +230,8 @@ struct Ana2Plan {
 };
 
 template <typename T, int LM>
-Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int off) {
+Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int off,
+                          int64_t xs) {
   using A = typename AccOf<T>::type;
   Ana2Plan<T, LM> pl;
   if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
@@ -237,7 +240,7 @@ Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int of
     constexpr int VW = 16 / static_cast<int>(sizeof(A));
     constexpr int V = ana_stream_v<A>();
     const int64_t n = L1.n_in, nc1 = L1.n_coef, n1 = L2.n_in, nc2 = L2.n_coef;
-    if (n < 1024 || n % VW || n > 0x3fffffffLL || nc2 < 1 || L1.a_len != n1 ||
+    if (n < 1024 || xs % VW || xs < n || xs > 0x3fffffffLL || nc2 < 1 || L1.a_len != n1 ||
         L2.a_len > nc2 + 1 || rows <= 0)
       return pl;
     const int mode = L1.mode, mode2 = L2.mode;
@@ -288,6 +291,8 @@ Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int of
     p.n1 = static_cast<int>(n1);
     p.nc2 = static_cast<int>(nc2);
     p.a_len2 = static_cast<int>(L2.a_len);
+    p.xs = static_cast<int>(xs);
+    p.n_al = static_cast<int>(n / VW * VW);
     p.off = off;
     p.mode = mode;
     p.mode2 = mode2;
@@ -307,24 +312,26 @@ Ana2Plan<T, LM> plan_ana2(int64_t rows, const Level& L1, const Level& L2, int of
   }
 }
 
-// Runs levels L1, L2 of an analysis in one streaming pass: x (rows x L1.n_in) -> details of both
-// levels (L1.detail, L2.detail) and the level-2 approximation a2_out (rows x L2.a_len).
-// FDWT_ERR_UNSUPPORTED when the pair does not fuse.
+// Runs levels L1, L2 of an analysis in one streaming pass: x (rows of L1.n_in samples, xs apart)
+// -> details of both levels (L1.detail, L2.detail) and the level-2 approximation a2_out (rows
+// of L2.a_len, as apart).  FDWT_ERR_UNSUPPORTED when the pair does not fuse.
 template <typename T, int LM>
-int run_ana2_stream(int64_t rows, const void* x, const Level& L1, const Level& L2, void* a2_out,
-                    const double* h0, const double* h1, int L, int off, cudaStream_t stream) {
+int run_ana2_stream(int64_t rows, const void* x, const Level& L1, const Level& L2, int64_t xs,
+                    void* a2_out, int64_t as, const double* h0, const double* h1, int L, int off,
+                    cudaStream_t stream) {
   using A = typename AccOf<T>::type;
   if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
     return FDWT_ERR_UNSUPPORTED;
   } else {
-    Ana2Plan<T, LM> pl = plan_ana2<T, LM>(rows, L1, L2, off);
-    if (!pl.ok || x == nullptr || a2_out == nullptr || L1.detail == nullptr ||
+    Ana2Plan<T, LM> pl = plan_ana2<T, LM>(rows, L1, L2, off, xs);
+    if (!pl.ok || as < L2.a_len || as > 0x3fffffffLL || x == nullptr || a2_out == nullptr || L1.detail == nullptr ||
         L2.detail == nullptr || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
       return FDWT_ERR_UNSUPPORTED;
     auto& p = pl.p;
     p.x = static_cast<const A*>(x);
     p.d1 = static_cast<A*>(L1.detail);
     p.a2 = static_cast<A*>(a2_out);
+    p.as = static_cast<int>(as);
     p.d2 = static_cast<A*>(L2.detail);
     p.err = device_error_flag();
     if (p.err == nullptr) return FDWT_ERR_CUDA;

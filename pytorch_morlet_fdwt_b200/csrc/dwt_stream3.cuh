@@ -27,17 +27,19 @@ namespace dwtk {
 
 template <typename A, int LM>
 struct Ana3Params {
-  const A* x;        // (rows, n)
+  const A* x;        // (rows, xs)
   A* d1;             // (rows, nc1) level-k details
   A* d2;             // (rows, nc2) level-(k+1) details
   A* d3;             // (rows, nc3) level-(k+2) details
-  A* a3;             // (rows, a_len3) level-(k+2) approximation
+  A* a3;             // (rows, as) level-(k+2) approximation
   int* err;          // device error word
   uint32_t dbg_tx;   // test hook: extra expected bytes of global tile 0's copy
   long long tries;   // poll limit of the main mbarrier waits
   int64_t ntile;     // rows * tiles
   int64_t P;         // period of level k's boundary mode on n
   int32_t n, nc1, nc2, nc3, a_len3, off, mode, tiles;
+  int32_t xs, as;    // row strides of x and of cA3 (xs a multiple of 16 bytes)
+  int32_t n_al;      // n rounded down to 16 bytes: the bulk copies end there
   int32_t span;      // x elements per ring slot
   int32_t T3;        // level-(k+2) outputs per tile (a multiple of V)
   int32_t K1, kh1;   // level-k items per tile, of which kh1 before the first owned detail
@@ -67,7 +69,7 @@ __device__ void ana3_tiles(const Ana3Params<A, LM>& p, A* ring, A* buf1, A* buf2
   auto ext_fill = [&](int64_t g, int s) {
     const int64_t row = g / p.tiles;
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
-    const A* xr = p.x + row * n;
+    const A* xr = p.x + row * p.xs;
     A* sl = slot(s);
     auto one = [&](int q) {
       const int64_t e = ext_index(q, n, p.mode, p.P);
@@ -76,16 +78,16 @@ __device__ void ana3_tiles(const Ana3Params<A, LM>& p, A* ring, A* buf1, A* buf2
     };
     const int l1 = min(xlo + span, 0), r1 = min(xlo + span, p.x_hi);
     for (int q = xlo + tid; q < l1; q += SNT) one(q);
-    for (int q = max(xlo, n) + tid; q < r1; q += SNT) one(q);
+    for (int q = max(xlo, p.n_al) + tid; q < r1; q += SNT) one(q);
     cp_async_commit();
   };
   auto issue = [&](int64_t g, int s) {
     const int64_t row = g / p.tiles;
     const int xlo = slot_lo(static_cast<int>(g % p.tiles));
-    const int lo = max(xlo, 0), hi = min(xlo + span, n);
+    const int lo = max(xlo, 0), hi = min(xlo + span, p.n_al);
     const unsigned bytes = static_cast<unsigned>(max(hi - lo, 0)) * sizeof(A);
     mbar_expect_tx(&bar[s], bytes + (g == 0 ? p.dbg_tx : 0u));
-    if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * n + lo, bytes, &bar[s]);
+    if (bytes) bulk_g2s(slot(s) + (lo - xlo), p.x + row * p.xs + lo, bytes, &bar[s]);
   };
   // zero mode: buffer cells of positions outside [0, nc) are the next level's zero extension
   auto zero_outside = [&](A* b, int cell0, int first, int cnt, int nc) {
@@ -158,7 +160,7 @@ __device__ void ana3_tiles(const Ana3Params<A, LM>& p, A* ring, A* buf1, A* buf2
       __syncthreads();
     }
     if (ok) {  // level k+2 from buffer 2
-      A* a3row = p.a3 + row * p.a_len3;
+      A* a3row = p.a3 + row * p.as;
       A* d3row = p.d3 + row * p.nc3;
 #pragma unroll 1
       for (int m = tid; m < T3 / V; m += SNT) {
@@ -241,7 +243,7 @@ struct Ana3Plan {
 // when the triple does not fuse.  Shape-only: the input pointer's alignment is the caller's check.
 template <typename T, int LM>
 Ana3Plan<T, LM> plan_ana3(int64_t rows, const Level& L1, const Level& L2, const Level& L3,
-                          int off) {
+                          int off, int64_t xs) {
   using A = typename AccOf<T>::type;
   Ana3Plan<T, LM> pl;
   if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
@@ -250,7 +252,7 @@ Ana3Plan<T, LM> plan_ana3(int64_t rows, const Level& L1, const Level& L2, const 
     constexpr int VW = 16 / static_cast<int>(sizeof(A));
     constexpr int V = ana_stream_v<A>();
     const int64_t n = L1.n_in, nc1 = L1.n_coef, nc2 = L2.n_coef, nc3 = L3.n_coef;
-    if (n < 4096 || n % VW || n > 0x3fffffffLL || nc3 < 1 || rows <= 0) return pl;
+    if (n < 4096 || xs % VW || xs < n || xs > 0x3fffffffLL || nc3 < 1 || rows <= 0) return pl;
     if (L1.a_len != L2.n_in || L2.a_len != L3.n_in || L3.a_len > nc3 + 1) return pl;
     const int mode = L1.mode;
     if (L2.mode != mode || L3.mode != mode) return pl;
@@ -301,6 +303,8 @@ Ana3Plan<T, LM> plan_ana3(int64_t rows, const Level& L1, const Level& L2, const 
     p.nc2 = static_cast<int>(nc2);
     p.nc3 = static_cast<int>(nc3);
     p.a_len3 = static_cast<int>(L3.a_len);
+    p.xs = static_cast<int>(xs);
+    p.n_al = static_cast<int>(n / VW * VW);
     p.off = off;
     p.mode = mode;
     p.tiles = static_cast<int>(tiles);
@@ -324,19 +328,19 @@ Ana3Plan<T, LM> plan_ana3(int64_t rows, const Level& L1, const Level& L2, const 
   }
 }
 
-// Runs levels L1, L2, L3 of an analysis in one streaming pass: x (rows x L1.n_in) -> the details
-// of all three levels and the level-3 approximation a3_out (rows x L3.a_len).
-// FDWT_ERR_UNSUPPORTED when the triple does not fuse.
+// Runs levels L1, L2, L3 of an analysis in one streaming pass: x (rows of L1.n_in samples, xs
+// apart) -> the details of all three levels and the level-3 approximation a3_out (rows of
+// L3.a_len, as apart).  FDWT_ERR_UNSUPPORTED when the triple does not fuse.
 template <typename T, int LM>
 int run_ana3_stream(int64_t rows, const void* x, const Level& L1, const Level& L2,
-                    const Level& L3, void* a3_out, const double* h0, const double* h1, int L,
-                    int off, cudaStream_t stream) {
+                    const Level& L3, int64_t xs, void* a3_out, int64_t as, const double* h0,
+                    const double* h1, int L, int off, cudaStream_t stream) {
   using A = typename AccOf<T>::type;
   if constexpr (!std::is_same<T, A>::value || LM > kStreamMaxLM) {
     return FDWT_ERR_UNSUPPORTED;
   } else {
-    Ana3Plan<T, LM> pl = plan_ana3<T, LM>(rows, L1, L2, L3, off);
-    if (!pl.ok || x == nullptr || a3_out == nullptr || L1.detail == nullptr ||
+    Ana3Plan<T, LM> pl = plan_ana3<T, LM>(rows, L1, L2, L3, off, xs);
+    if (!pl.ok || as < L3.a_len || as > 0x3fffffffLL || x == nullptr || a3_out == nullptr || L1.detail == nullptr ||
         L2.detail == nullptr || L3.detail == nullptr ||
         (reinterpret_cast<uintptr_t>(x) & 15) != 0)
       return FDWT_ERR_UNSUPPORTED;
@@ -346,6 +350,7 @@ int run_ana3_stream(int64_t rows, const void* x, const Level& L1, const Level& L
     p.d2 = static_cast<A*>(L2.detail);
     p.d3 = static_cast<A*>(L3.detail);
     p.a3 = static_cast<A*>(a3_out);
+    p.as = static_cast<int>(as);
     p.err = device_error_flag();
     if (p.err == nullptr) return FDWT_ERR_CUDA;
     {

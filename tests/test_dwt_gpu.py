@@ -354,3 +354,26 @@ def test_misaligned_rows_on_a_multi_launch_length(mode):
         close(g, r, 1e-5)
     y = F.waverec(got, bank, mode)
     close(y[..., :n], x, 1e-5)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.float64, 1e-12)])
+@pytest.mark.parametrize("mode", ["zero", "periodic", "symmetric", "reflect"])
+@pytest.mark.parametrize("wname", ["haar", "db3", "db8", "db12"])
+def test_padded_handovers_between_streaming_stages(wname, mode, dtype, tol):
+    """Coefficient lengths are odd in every mode but periodization, so the approximation one
+    streaming pass hands to the next is stored in the workspace with its rows rounded up to 16
+    bytes; the next pass bulk-copies up to the last 16-byte boundary of each row and gathers the
+    ragged end.  Every row of every level against the oracle, at lengths whose intermediate
+    approximations take every residue mod 16 bytes, then the round trip."""
+    torch.manual_seed(31)
+    bank = F.get_filter_bank(wname)
+    tb = (bank.dec_lo, bank.dec_hi, bank.rec_lo, bank.rec_hi)
+    for n in (16384, 20004, 24584):
+        x = torch.randn(6, n, device=DEV, dtype=dtype)
+        level = min(7, F.dwt_max_level(n, wname))
+        got = F.wavedec(x, bank, mode, level)
+        ref = D.wavedec(x.double().cpu().numpy(), tb, mode, level)
+        for g, r in zip(got, ref):
+            close(g, r, tol)
+        y = F.waverec(got, bank, mode)
+        close(y[..., :n], x, tol)
